@@ -1,0 +1,314 @@
+"""Benchmark of the connectome recurrence on B200: 6-step light-cone forward, float16 deviation.
+
+    python bench.py [--gpus N --steps K --warmup W] [--batch B] [--impl ours|reference]
+
+Workload (configuration 3): the full-scale synthetic connectome (166,700 neurons, ~10.5M synapses;
+``alphafly_b200.synth.full``), inputs = 17,937 sensory neurons, outputs = 2,333, 6 steps, light-cone
+pruned, float16 deviation from the float32 resting trajectory, B = 35,840 positions per GPU.
+A "step" is one ``ConnectomeRNN.forward_io`` over the batch.  With N GPUs (torchrun, one process
+per GPU) every rank evaluates its own 35,840 positions with the wiring replicated: no collective on
+the data path, weak scaling.  ``value`` = positions evaluated by all ranks / max-over-ranks device
+time of the K timed steps (inputs resident in HBM); ``e2e`` = the same through the public call with
+the drive in pinned host memory and the output copied back inside the timed region.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the float32 port in
+oracle/, all host threads) on a bounded sample of the same workload and prints the same line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "connectome evals/sec (6-step fwd) at 1/2/4/8 B200; % of HBM roofline"
+UNIT = "positions/s"
+STEPS_T = 6
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=35_840, help="positions per GPU")
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    path = os.path.join(HERE, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        d = json.load(open(path))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def workload(seed=0):
+    from alphafly_b200 import synth
+    return synth.full(seed)
+
+
+def algorithmic_bytes(rows_len, nnz, n_fed, batch, n_out, s_state=2, s_val=2, s_idx=4, row_const=10):
+    """Compulsory HBM bytes of one 6-step forward of ``batch`` positions: per step t the sub-matrix
+    (nnz_t (index + value) + row pointer), the gathered state R_{t-1} x B read once, the new state R_t x B
+    written once, the fed input rows U_t x B read once, the per-row constants; plus the float32 output."""
+    per_step = []
+    for t in range(1, len(rows_len)):
+        b = nnz[t] * (s_idx + s_val) + 4 * (rows_len[t] + 1) + batch * s_state * (rows_len[t - 1] + rows_len[t] + n_fed[t]) \
+            + row_const * rows_len[t]
+        per_step.append(b)
+    return per_step, sum(per_step) + n_out * batch * 4
+
+
+class Clocks:
+    """nvidia-smi samples of the SM clock and throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.rows, self.proc = index, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            for k, name in enumerate(names):
+                if len(r) > 5 + k and r[5 + k].lower().startswith("active"):
+                    reasons.add(name)
+        loaded = sorted(sm)[len(sm) // 2:] if sm else []
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.rows)}
+
+
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and args.impl == "ours":
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                             device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def cpu_sample(inst, seconds, batch=16):
+    """The oracle's float32 forward (OpenMP, all host threads) on ``batch`` positions, repeated for about
+    ``seconds``; returns (positions/s, threads, description)."""
+    from alphafly_b200 import synth
+    from oracle import oracle as orc
+    fwd = orc.CpuForward(inst.n, inst.conn.pre.numpy(), inst.conn.post.numpy(), inst.conn.sign.numpy(), inst.w0.numpy(),
+                         inst.log_gain.numpy(), inst.bias.numpy(), inst.alpha_logit.numpy(), inst.in_idx.numpy(),
+                         inst.out_idx.numpy(), STEPS_T)
+    u = synth.drive(inst, batch, seed=123)
+    fwd(u)                                                   # warm-up
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        fwd(u)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    threads = orc.lib().ref_num_threads()
+    return reps * batch / el, threads, (f"{reps} x {batch} positions of configuration 3's graph, float32 light-cone "
+                                        f"forward (oracle port of the reference), {el:.1f} s")
+
+
+def reference_arm(args, rank, world):
+    if rank != 0:
+        return
+    inst = workload()
+    per_step = []
+    from oracle import oracle as orc
+    from alphafly_b200 import synth
+    batch = 16
+    fwd = orc.CpuForward(inst.n, inst.conn.pre.numpy(), inst.conn.post.numpy(), inst.conn.sign.numpy(), inst.w0.numpy(),
+                         inst.log_gain.numpy(), inst.bias.numpy(), inst.alpha_logit.numpy(), inst.in_idx.numpy(),
+                         inst.out_idx.numpy(), STEPS_T)
+    u = synth.drive(inst, batch, seed=123)
+    for _ in range(args.warmup):
+        fwd(u)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        t = time.perf_counter()
+        fwd(u)
+        per_step.append(time.perf_counter() - t)
+    el = time.perf_counter() - t0
+    value = args.steps * batch / el
+    threads = orc.lib().ref_num_threads()
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config3: full-scale synthetic connectome, 6-step light-cone forward",
+                       "batch_per_step": batch, "note": "each step is a bounded sample of the GPU arm's 35,840-position batch"},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": f"{batch} positions per step, float32, oracle port of chessfly/brain.py forward_io"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank, world, local = init_dist(args)
+    if args.impl == "reference":
+        return reference_arm(args, rank, world)
+    from alphafly_b200 import synth
+    from alphafly_b200.brain import ConnectomeRNN
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    inst = workload()
+    rnn = ConnectomeRNN(inst.conn)
+    synth.apply(rnn, inst)
+    rnn = rnn.to(dev)
+    in_idx, out_idx = inst.in_idx.to(dev), inst.out_idx.to(dev)
+    B = args.batch
+    # this rank's shard of positions: its own seed
+    u_host = torch.from_numpy(synth.drive(inst, min(B, 2048), seed=1000 + rank)).half()
+    reps = (B + u_host.shape[1] - 1) // u_host.shape[1]
+    u_host = u_host.repeat(1, reps)[:, :B].contiguous()
+    u = u_host.to(dev)
+    cone = rnn.light_cone(in_idx, out_idx, STEPS_T)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    def max_over_ranks(x):
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        if world > 1:
+            torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
+
+    with torch.no_grad():
+        for _ in range(args.warmup):
+            out = rnn.forward_io(u, in_idx, out_idx, STEPS_T)
+        barrier()
+        # per-launch events on the launching stream: T step kernels + the output kernel, every timed step
+        ev = [[torch.cuda.Event(enable_timing=True) for _ in range(STEPS_T + 2)] for _ in range(args.steps)]
+        for row in ev:
+            for e in row:
+                e.record(stream)                               # creates the handles
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        with Clocks(local) as clocks:
+            start.record(stream)
+            for k in range(args.steps):
+                out = cone.forward(1, u, events=ev[k])         # == rnn.forward_io(u16, ...) with the cache warm
+            stop.record(stream)
+            barrier()
+        dev_ms = start.elapsed_time(stop)
+        step_ms = [[ev[k][t].elapsed_time(ev[k][t + 1]) for t in range(STEPS_T + 1)] for k in range(args.steps)]
+    ms = max_over_ranks(dev_ms)
+    value = world * B * args.steps / (ms / 1000.0)
+
+    # roofline of the step kernel: algorithmic bytes / its measured duration
+    hbm, peak_kind = peaks()
+    fed = [0] + [len(x) for x in cone.u_pos[1:]]
+    per_step_bytes, total_bytes = algorithmic_bytes(cone.rows_len, cone.nnz, fed, B, len(inst.out_idx))
+    kernel_ms = [sum(s[t] for s in step_ms) / args.steps for t in range(STEPS_T)]
+    kernel_total_ms = sum(kernel_ms)
+    achieved = sum(per_step_bytes) / (kernel_total_ms / 1000.0) / 1e9
+    gathered = sum(cone.nnz) * B * 2                          # state bytes the SpMM pulls through L2 per forward
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
+                "traffic": None, "kernel": "step_kernel<__half,__half> (6 launches per forward)",
+                "algorithmic_bytes_per_launch": int(sum(per_step_bytes) / STEPS_T),
+                "launch_ms": [round(x, 3) for x in kernel_ms],
+                "l2_gather_bytes_per_forward": int(gathered),
+                "l2_gather_gbs": round(gathered / (kernel_total_ms / 1000.0) / 1e9, 1)}
+
+    e2e = None
+    if not args.no_e2e:
+        pin_u = u_host.pin_memory()
+        pin_out = torch.empty(len(inst.out_idx), B, dtype=torch.float32).pin_memory()
+        u_dev = torch.empty_like(u)
+        with torch.no_grad():
+            for _ in range(2):
+                u_dev.copy_(pin_u, non_blocking=True)
+                pin_out.copy_(rnn.forward_io(u_dev, in_idx, out_idx, STEPS_T), non_blocking=True)
+            barrier()
+            s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s0.record(stream)
+            for _ in range(args.steps):
+                u_dev.copy_(pin_u, non_blocking=True)
+                pin_out.copy_(rnn.forward_io(u_dev, in_idx, out_idx, STEPS_T), non_blocking=True)
+            s1.record(stream)
+            barrier()
+        e2e_ms = max_over_ranks(s0.elapsed_time(s1))
+        e2e = {"value": world * B * args.steps / (e2e_ms / 1000.0), "unit": UNIT,
+               "h2d_bytes_per_step": pin_u.numel() * pin_u.element_size(),
+               "d2h_bytes_per_step": pin_out.numel() * pin_out.element_size(),
+               "ms_per_step": e2e_ms / args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, threads, desc = cpu_sample(inst, args.cpu_seconds)
+        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+
+    if world > 1:
+        torch.distributed.barrier()
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                "config": {"workload": "config3: full-scale synthetic connectome (166,700 neurons, "
+                                       f"{inst.e:,} synapses), 6-step light-cone forward, float16 deviation",
+                           "positions_per_gpu": B, "global_positions": B * world, "l2": "inputs larger than L2",
+                           "parallelism": f"positions sharded over {world} GPU(s), wiring replicated, no collective"},
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+                "gpu_launches": args.steps * (STEPS_T + 1),
+                "light_cone": {"rows": cone.rows_len, "nnz": cone.nnz, "edge_visits": cone.edge_visits}}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,42 @@
+"""The C ABI: every entry point declared in include/afb.h is exported by libafb.so and bound by the
+Python host, and argument errors come back as AfbError without touching a GPU."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared():
+    text = open(os.path.join(ROOT, "include", "afb.h")).read()
+    return sorted(set(re.findall(r"AFB_API\s+[\w\s\*]*?\b(afb_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared()
+    assert "afb_cone_forward" in names and "afb_cone_create" in names and len(names) >= 16
+
+
+def test_library_exports_every_declared_symbol():
+    from alphafly_b200 import _lib
+    lib = _lib.load()
+    for name in declared():
+        assert hasattr(lib, name), name
+        assert name in _lib.SIGNATURES, f"{name} has no Python binding"
+    assert lib.afb_compiled_arch() == 100 and lib.afb_version() >= 1
+
+
+def test_argument_errors_are_reported_without_a_gpu():
+    from alphafly_b200 import _lib
+    lib = _lib.load()
+    h = ctypes.c_void_p()
+    rc = lib.afb_cone_create(ctypes.byref(h), 0, 0, None, None, None, 0, None, 1, 6, None)
+    assert rc == _lib.EINVAL and b"n must be" in lib.afb_last_error()
+    with pytest.raises(_lib.AfbError, match="steps must be"):
+        _lib.check(lib.afb_cone_create(ctypes.byref(h), 10, 0, None, None, None, 0, ctypes.c_void_p(8), 1, 0, None))
+    assert lib.afb_cone_forward_workspace(None, 0, 64) == 0
+    with pytest.raises(_lib.AfbError, match="unknown mode"):
+        _lib.check(lib.afb_cone_forward(ctypes.c_void_p(16), 7, None, 0, 0, None, 0, None, 0, None))

@@ -1,0 +1,246 @@
+"""Parity of the CUDA forward path with the reference, through the package's module API.
+
+Light-cone indices must be bit-exact (against the reference's own arrays or their SHA-256 in
+tests/golden/).  float32 outputs must be within 1e-4 relative L2 of the reference (north-star gate;
+in practice they are ~1e-7).  The float16-deviation path must be within 2e-3 relative L2 of float32
+with >= 99.5% policy-argmax agreement, and within the reference's own test bound
+(tests/test_core.py:491-511).
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import oracle as orc
+from test_oracle import check_cone_arrays, check_cone_hashes
+from alphafly_b200 import synth
+from alphafly_b200.brain import ConnectomeRNN
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+F32_GATE = 1e-4
+F16_GATE = 2e-3
+
+
+def rnn_for(inst, **kw):
+    rnn = ConnectomeRNN(inst.conn, **kw)
+    synth.apply(rnn, inst)
+    return rnn.to(DEV)
+
+
+class NpCone:
+    """A LightCone's tensors as numpy arrays, in the oracle's field layout."""
+
+    def __init__(self, cone):
+        to = lambda x: None if x is None else x.cpu().numpy()
+        self.steps = cone.steps
+        self.rows = [to(r) for r in cone.rows]
+        self.ops = [None if op is None else type("Op", (), {k: to(getattr(op, k)) for k in
+                                                          ("edges", "post", "pre", "crow", "t_order", "t_crow", "t_col")})
+                    for op in cone.ops]
+        self.carried = [None] + [to(c).squeeze(1) for c in cone.carried[1:]]
+        for name in ("keep_next", "keep_prev", "prev_row", "u_pos", "u_src"):
+            setattr(self, name, [None] + [to(x) for x in getattr(cone, name)[1:]])
+        self.out_pos, self.out_src, self.edge_visits = to(cone.out_pos), to(cone.out_src), cone.edge_visits
+
+
+@pytest.fixture(scope="module")
+def small():
+    inst = synth.small()
+    return inst, rnn_for(inst)
+
+
+@pytest.fixture(scope="module")
+def full():
+    inst = synth.full()
+    return inst, rnn_for(inst)
+
+
+@pytest.mark.parametrize("steps", [1, 2, 4, 6])
+def test_light_cone_fields_equal_the_reference_tiny(steps):
+    g = golden("tiny")
+    conn = synth.tiny(120, 700, seed=3)
+    rnn = ConnectomeRNN(conn, global_scale=3.0, bias_init=0.1).to(DEV)
+    cone = rnn.light_cone(torch.as_tensor(g["cone_in_idx"], device=DEV), torch.as_tensor(g["cone_out_idx"], device=DEV),
+                          steps)
+    check_cone_arrays(NpCone(cone), g, f"cone{steps}")
+    assert len(cone.rows[0]) == 0
+
+
+@pytest.mark.parametrize("config", ["small", "shuffled"])
+def test_light_cone_hashes_equal_the_reference(config):
+    g = golden(config)
+    inst = synth.small() if config == "small" else synth.shuffled()
+    rnn = rnn_for(inst)
+    cone = rnn.light_cone(inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+    check_cone_hashes(NpCone(cone), g)
+
+
+def test_light_cone_hashes_equal_the_reference_full(full):
+    inst, rnn = full
+    cone = rnn.light_cone(inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+    check_cone_hashes(NpCone(cone), golden("full"))
+
+
+def test_tiny_forward_io_float32_matches_reference():
+    """The reference's light-cone test graph (float64 there): outputs of the CUDA float32 path."""
+    g = golden("tiny")
+    conn = synth.tiny(120, 700, seed=3)
+    rnn = ConnectomeRNN(conn, global_scale=3.0, bias_init=0.1)
+    with torch.no_grad():
+        rnn.log_gain.copy_(torch.from_numpy(g["cone_log_gain"]))
+        rnn.bias.copy_(torch.from_numpy(g["cone_bias"]))
+        rnn.alpha_logit.copy_(torch.from_numpy(g["cone_alpha_logit"]))
+    rnn = rnn.to(DEV)
+    in_idx, out_idx = torch.as_tensor(g["cone_in_idx"], device=DEV), torch.as_tensor(g["cone_out_idx"], device=DEV)
+    with torch.no_grad():
+        for steps in (1, 2, 4, 6):
+            u = torch.as_tensor(g[f"s{steps}_u_in"], dtype=torch.float32, device=DEV)
+            out = rnn.forward_io(u, in_idx, out_idx, steps)
+            assert out.dtype == torch.float32 and out.shape == (20, 5)
+            assert orc.rel_l2(out.cpu().numpy(), g[f"s{steps}_out"]) < 1e-6, steps
+
+
+def test_small_forward_io_float32_matches_reference(small):
+    inst, rnn = small
+    g = golden("small")
+    u = torch.from_numpy(synth.drive(inst, 64, seed=0)).to(DEV)
+    with torch.no_grad():
+        out = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6).cpu().numpy()
+    err = orc.rel_l2(out, g["fwd_io_f64"])
+    assert err < F32_GATE, err
+    assert orc.rel_l2(out, g["fwd_io_f32"]) < F32_GATE
+
+
+def test_small_literal_forward_matches_reference(small):
+    inst, rnn = small
+    g = golden("small")
+    u = torch.from_numpy(synth.drive(inst, 64, seed=0))
+    full = torch.zeros(inst.n, 64).index_copy_(0, inst.in_idx, u).to(DEV)
+    with torch.no_grad():
+        h = rnn(full.contiguous(), 6)
+    assert h.shape == (inst.n, 64)
+    err = orc.rel_l2(h[inst.out_idx.to(DEV)].cpu().numpy(), g["fwd_full_f32"])
+    assert err < F32_GATE, err
+
+
+def test_shuffled_forward_io_float32_matches_reference():
+    inst = synth.shuffled()
+    rnn = rnn_for(inst)
+    g = golden("shuffled")
+    u = torch.from_numpy(synth.drive(inst, 16, seed=3)).to(DEV)
+    with torch.no_grad():
+        out = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6).cpu().numpy()
+    assert orc.rel_l2(out, g["fwd_io_f32"]) < F32_GATE
+
+
+def test_full_forward_io_and_literal_forward_match_reference(full):
+    inst, rnn = full
+    g = golden("full")
+    with torch.no_grad():
+        u = torch.from_numpy(synth.drive(inst, 8, seed=0)).to(DEV)
+        out = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6).cpu().numpy()
+        assert orc.rel_l2(out, g["fwd_io_f32"]) < F32_GATE
+        u4 = torch.from_numpy(synth.drive(inst, 4, seed=1))
+        fullu = torch.zeros(inst.n, 4).index_copy_(0, inst.in_idx, u4).to(DEV)
+        h = rnn(fullu.contiguous(), 6)[inst.out_idx.to(DEV)].cpu().numpy()
+    assert orc.rel_l2(h, g["fwd_full_f32"]) < F32_GATE
+
+
+def policy_logits(out: np.ndarray, n_out: int) -> np.ndarray:
+    """Random readout after per-neuron standardisation (the reference's RunningNorm in spirit)."""
+    heads = synth.head_weights(n_out)
+    r = out.T.astype(np.float64)
+    r = np.clip((r - r.mean(0)) / np.sqrt(r.var(0) + 1e-8), -8, 8)
+    return r @ heads["policy.weight"].T.astype(np.float64)
+
+
+@pytest.mark.parametrize("config", ["small", "full"])
+def test_float16_deviation_matches_float32(config, small, full):
+    inst, rnn = small if config == "small" else full
+    batch = 256
+    u = torch.from_numpy(synth.drive(inst, batch, seed=7)).to(DEV)
+    with torch.no_grad():
+        ref = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+        half = rnn.forward_io(u.half(), inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+    assert half.dtype == torch.float32
+    ref, half = ref.cpu().numpy(), half.cpu().numpy()
+    err = orc.rel_l2(half, ref)
+    assert err < F16_GATE, err
+    # the position-dependent part too, not just the resting pattern it sits on
+    dev_ref, dev_half = ref - ref.mean(1, keepdims=True), half - half.mean(1, keepdims=True)
+    assert orc.rel_l2(dev_half, dev_ref) < 0.05
+    agree = (policy_logits(half, len(inst.out_idx)).argmax(1) == policy_logits(ref, len(inst.out_idx)).argmax(1)).mean()
+    assert agree >= 0.995, agree
+
+
+def test_float16_deviation_reference_bound_with_clamped_rows():
+    """tests/test_core.py:491-511: a small signal on a large resting state, rows on both clamps."""
+    rnn = ConnectomeRNN(synth.tiny(400, 9000, seed=5), global_scale=2.0, bias_init=0.6)
+    g = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        rnn.log_gain.add_(torch.randn(rnn.log_gain.shape, generator=g) * 0.8)
+        rnn.bias.add_(torch.randn(rnn.bias.shape, generator=g) * 0.7)
+        rnn.bias[::17] += 12.0
+        rnn.alpha_logit.add_(torch.randn(rnn.alpha_logit.shape, generator=g))
+    rnn = rnn.to(DEV)
+    in_idx, out_idx = torch.arange(0, 40, device=DEV), torch.arange(300, 400, device=DEV)
+    u = (torch.randn(40, 64, generator=g) * 0.05).to(DEV)
+    with torch.no_grad():
+        for steps in (1, 3, 6):
+            ref = rnn.forward_io(u, in_idx, out_idx, steps)
+            half = rnn.forward_io(u.half(), in_idx, out_idx, steps)
+            signal = (ref - ref.mean(1, keepdim=True)).abs().mean()
+            assert float((half - ref).abs().max()) < 0.02 * float(signal) + 1e-4, steps
+
+
+@pytest.mark.parametrize("batch", [1, 5, 37, 128, 200])
+def test_ragged_batches_match_the_oracle(small, batch):
+    """Batch widths that are not a multiple of the kernel's 64/128-column tile, and B = 1."""
+    inst, rnn = small
+    pre, post = inst.conn.pre.numpy(), inst.conn.post.numpy()
+    cone = orc.light_cone(inst.n, pre, post, inst.in_idx.numpy(), inst.out_idx.numpy(), 6)
+    w = orc.edge_weights(inst.conn.sign.numpy(), inst.w0.numpy(), inst.log_gain.numpy())
+    alpha = orc.sigmoid(inst.alpha_logit.numpy().astype(np.float64))
+    u = synth.drive(inst, batch, seed=batch)
+    ref = orc.forward_io(orc.full_csr(inst.n, pre, post), cone, w, inst.bias.numpy().astype(np.float64), alpha,
+                         u.astype(np.float64))
+    with torch.no_grad():
+        out32 = rnn.forward_io(torch.from_numpy(u).to(DEV), inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+        out16 = rnn.forward_io(torch.from_numpy(u).to(DEV).half(), inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+    assert out32.shape == (len(inst.out_idx), batch)
+    assert orc.rel_l2(out32.cpu().numpy(), ref) < F32_GATE
+    assert orc.rel_l2(out16.cpu().numpy(), ref) < F16_GATE
+
+
+def test_strided_input_and_weight_updates_invalidate_the_cache(small):
+    inst, rnn = small
+    u = torch.from_numpy(synth.drive(inst, 64, seed=1)).to(DEV)
+    wide = torch.zeros(len(inst.in_idx), 96, device=DEV)
+    wide[:, :64] = u
+    with torch.no_grad():
+        a = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+        b = rnn.forward_io(wide[:, :64], inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+        torch.testing.assert_close(a, b, rtol=0, atol=0)
+        rnn.bias.add_(0.05)                                    # in-place update bumps the version
+        c = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+        rnn.bias.sub_(0.05)
+        d = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
+    assert not torch.allclose(a, c)
+    torch.testing.assert_close(a, d, rtol=1e-6, atol=1e-6)
+
+
+def test_columns_are_independent_at_full_batch(full):
+    """Size-independent property at the benchmark's batch: each position's output depends only on its
+    own column, so a 35,840-wide float16 run equals narrow runs of the same columns."""
+    inst, rnn = full
+    u = torch.from_numpy(synth.drive(inst, 512, seed=11)).to(DEV).half()
+    big = u.repeat(1, 70)                                     # 35,840 columns
+    in_idx, out_idx = inst.in_idx.to(DEV), inst.out_idx.to(DEV)
+    with torch.no_grad():
+        wide = rnn.forward_io(big, in_idx, out_idx, 6)
+        narrow = rnn.forward_io(u, in_idx, out_idx, 6)
+    assert wide.shape == (len(inst.out_idx), 35840)
+    for k in (0, 33, 69):
+        torch.testing.assert_close(wide[:, k * 512:(k + 1) * 512], narrow, rtol=0, atol=0)
