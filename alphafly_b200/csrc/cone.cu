@@ -181,6 +181,7 @@ void build_schedule(Csr &m, cudaStream_t s) {
     to_device(m.item_rows.get(), starts, s);
     m.item_order.alloc(order.size());
     to_device(m.item_order.get(), order, s);
+    build_bounds(m, s);
 }
 
 }  // namespace afb

@@ -200,7 +200,7 @@ int afb_cone_resting(const afb_cone *c, int t, float *dst, void *stream) {
 size_t afb_cone_forward_workspace(const afb_cone *c, int mode, int64_t batch) {
     if (!c || batch < 0 || (mode != AFB_MODE_F32 && mode != AFB_MODE_DEV16)) return 0;
     const size_t es = mode == AFB_MODE_F32 ? 4 : 2;
-    return 2 * align256((size_t)c->max_rows * padded_ld(batch) * es) + 256;
+    return 2 * align256((size_t)c->max_rows * padded_ld(batch, (int)es) * es) + 256;
 }
 
 int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_t ld_u, int64_t batch, float *out,
@@ -219,12 +219,14 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
         check_aligned(workspace, 256, "workspace");
         cudaStream_t s = as_stream(stream);
         const size_t es = mode == AFB_MODE_F32 ? 4 : 2;
-        const int64_t ld = padded_ld(batch);
+        const int64_t ld = padded_ld(batch, (int)es);
         char *ws = static_cast<char *>(workspace);
         void *buf[2] = {ws, ws + align256((size_t)c->max_rows * ld * es)};
         const int vec = mode == AFB_MODE_F32 ? 4 : 8;
         const int u_vec_ok = (ld_u % vec == 0) && (reinterpret_cast<uintptr_t>(u_in) % 16 == 0);
         const void *x_in = nullptr;
+        const int64_t bt = tile_cols((int)es);
+        int64_t ts_in = 0;
         for (int t = 1; t <= c->steps; ++t) {
             const Step &sp = c->st[t];
             StepArgs a{};
@@ -233,24 +235,26 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
             a.val = mode == AFB_MODE_F32 ? (const void *)sp.val32.get() : (const void *)sp.val16.get();
             a.item_rows = sp.op.item_rows.get();
             a.item_order = sp.op.item_order.get();
+            a.bounds = sp.op.bounds.get();
             a.n_items = sp.op.n_items;
             a.rc = sp.rc[mode].get();
             a.x_in = x_in ? x_in : buf[(t + 1) & 1];   // step 1 reads no state (R_0 is empty)
-            a.ld_in = ld;
+            a.ts_in = ts_in;
             a.u = u_in;
             a.ld_u = ld_u;
             a.u_vec_ok = u_vec_ok;
             a.x_out = buf[t & 1];
-            a.ld_out = ld;
+            a.ts_out = (int64_t)sp.n_rows * bt;
             a.batch = batch;
             if (events) AFB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[t - 1]), s));
             if (mode == AFB_MODE_F32) launch_step_f32(a, s);
             else launch_step_dev16(a, s);
             x_in = buf[t & 1];
+            ts_in = a.ts_out;
         }
         if (events) AFB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[c->steps]), s));
         launch_output((int)c->n_out, c->out_row.get(), c->out_base[mode].get(), mode == AFB_MODE_DEV16, x_in,
-                      mode == AFB_MODE_DEV16, ld, out, ld_out, batch, s);
+                      mode == AFB_MODE_DEV16, ts_in, out, ld_out, batch, s);
         if (events) AFB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[c->steps + 1]), s));
     });
 }
@@ -262,7 +266,7 @@ int afb_cone_forward(const afb_cone *c, int mode, const void *u_in, int64_t ld_u
 
 size_t afb_graph_forward_workspace(const afb_graph *g, int64_t batch) {
     if (!g || batch < 0) return 0;
-    return 2 * align256((size_t)g->n * padded_ld(batch) * 4) + 2 * align256((size_t)g->n * sizeof(RowConst)) + 256;
+    return 2 * align256((size_t)g->n * padded_ld(batch, 4) * 4) + 2 * align256((size_t)g->n * sizeof(RowConst)) + 256;
 }
 
 int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, const float *alpha_logit, float h_max,
@@ -278,7 +282,7 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
         AFB_CHECK(u, "u is NULL");
         check_aligned(workspace, 256, "workspace");
         cudaStream_t s = as_stream(stream);
-        const int64_t n = g->n, ld = padded_ld(batch);
+        const int64_t n = g->n, ld = padded_ld(batch, 4);
         char *ws = static_cast<char *>(workspace);
         const size_t sb = align256((size_t)n * ld * 4);
         void *buf[2] = {ws, ws + sb};
@@ -292,6 +296,7 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
         }
         const int u_vec_ok = (ld_u % 4 == 0) && (reinterpret_cast<uintptr_t>(u) % 16 == 0);
         const void *x_in = buf[1];
+        const int64_t ts = n * tile_cols(4);
         for (int t = 1; t <= steps; ++t) {
             const Csr &m = t == 1 ? g->empty : g->full;
             StepArgs a{};
@@ -300,20 +305,21 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
             a.val = w;
             a.item_rows = m.item_rows.get();
             a.item_order = m.item_order.get();
+            a.bounds = m.bounds.get();
             a.n_items = m.n_items;
             a.rc = t == 1 ? rc_first : rc_rest;
             a.x_in = x_in;
-            a.ld_in = ld;
+            a.ts_in = ts;
             a.u = u;
             a.ld_u = ld_u;
             a.u_vec_ok = u_vec_ok;
             a.x_out = buf[t & 1];
-            a.ld_out = ld;
+            a.ts_out = ts;
             a.batch = batch;
             launch_step_f32(a, s);
             x_in = buf[t & 1];
         }
-        launch_output((int)n, nullptr, nullptr, 0, x_in, 0, ld, h, ld_h, batch, s);   // row-for-row copy
+        launch_output((int)n, nullptr, nullptr, 0, x_in, 0, ts, h, ld_h, batch, s);   // row-for-row copy
     });
 }
 

@@ -30,6 +30,7 @@ struct Csr {
     int n_items = 0;
     DevBuf<int> item_rows;         // (n_items + 1) row boundaries
     DevBuf<int> item_order;        // (n_items) launch order
+    DevBuf<int2> bounds;           // (n_items x (warps + 1)) merge-path cut of each item over the CTA's warps
 };
 
 struct Step {
@@ -45,12 +46,21 @@ struct Step {
     DevBuf<__half> val16;          // half(w[edges]), AFB_MODE_DEV16
 };
 
+// Compile-time tuning of the step kernel (defaults are the shipped configuration).
+#ifndef AFB_LPE
+#define AFB_LPE 16
+#endif
+#ifndef AFB_ITEM_COST
+#define AFB_ITEM_COST 4096
+#endif
+
 // Schedule target: cost units (edges + kRowCost per row) per CTA work item.
 constexpr int kRowCost = 4;
-constexpr int kItemCost = 1024;
+constexpr int kItemCost = AFB_ITEM_COST;
 
-// Builds the item schedule of `m` from its crow (device); synchronous.
+// Builds the item schedule of `m` from its crow (device), then its merge-path table; synchronous.
 void build_schedule(Csr &m, cudaStream_t s);
+void build_bounds(Csr &m, cudaStream_t s);
 
 // Launch helpers of the fused step kernel (step.cu).
 struct StepArgs {
@@ -59,29 +69,35 @@ struct StepArgs {
     const void *val;
     const int *item_rows;
     const int *item_order;
+    const int2 *bounds;
     int n_items;
     const RowConst *rc;
-    const void *x_in;
-    int64_t ld_in;
-    const void *u;
+    const void *x_in;              // state of R_{t-1}, tile-major (see tile_cols)
+    int64_t ts_in;                 // elements between consecutive batch tiles of x_in
+    const void *u;                 // drive (n_in, batch), row-major with ld_u
     int64_t ld_u;
     int u_vec_ok;
-    void *x_out;
-    int64_t ld_out;
+    void *x_out;                   // state of R_t, tile-major
+    int64_t ts_out;
     int64_t batch;
 };
 
-// Batch columns handled per CTA (the state's leading dimension is padded to a multiple of this).
-constexpr int kBatchAlign = 128;
-inline int64_t padded_ld(int64_t batch) { return (batch + kBatchAlign - 1) / kBatchAlign * kBatchAlign; }
+// Batch columns one CTA covers for a state element of `elem_bytes`; the state's leading dimension is
+// padded to a multiple of it.
+int tile_cols(int elem_bytes);
+inline int64_t padded_ld(int64_t batch, int elem_bytes) {
+    const int64_t t = tile_cols(elem_bytes);
+    return (batch + t - 1) / t * t;
+}
 
 void launch_step_f32(const StepArgs &a, cudaStream_t s);
 void launch_step_dev16(const StepArgs &a, cudaStream_t s);
 
-// out[o, b] = src[o] >= 0 ? (add_base ? base[o] : 0) + state[src[o], b] : base[o]   (float32 out);
-// src NULL: row o of the state (or, with state NULL too, base[o] / zero); base NULL: zero.
+// out[o, b] = src[o] >= 0 ? (add_base ? base[o] : 0) + state[src[o], b] : base[o]   (float32 out, row-major);
+// src NULL: row o of the state (or, with state NULL too, base[o] / zero); base NULL: zero.  The state is
+// tile-major with tile stride ts_state.
 void launch_output(int n_out, const int *src, const float *base, int add_base, const void *state, int state_is_half,
-                   int64_t ld_state, float *out, int64_t ld_out, int64_t batch, cudaStream_t s);
+                   int64_t ts_state, float *out, int64_t ld_out, int64_t batch, cudaStream_t s);
 
 // Warp-per-row y = A x for one column vector (float32), A given by (crow, col, val).
 void launch_spmv(int n_rows, const int *crow, const int *col, const float *val, const float *x, float *y,

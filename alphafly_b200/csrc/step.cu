@@ -1,9 +1,9 @@
 // The fused light-cone step: one CSR SpMM over a batch tile with the whole state update in its
 // epilogue (chessfly/brain.py:273-277 float16 deviation, brain.py:310-314 float32).
 //
-// Layout.  State and drive are (rows, batch) row-major; a CTA owns one batch tile of kTile = 16
-// lanes x 16 bytes (128 half or 64 float columns) and one "item" -- a contiguous run of rows whose
-// cost (edges + 4 per row) is about kItemCost.  blockIdx.x = tile * n_items + k, so all items of a
+// Layout.  State and drive are (rows, batch) row-major; a CTA owns one batch tile of kLanesPerEdge
+// lanes x 16 bytes (with 16 lanes: 128 half or 64 float columns) and one "item" -- a contiguous run of
+// rows whose cost (edges + 4 per row) is about kItemCost.  blockIdx.x = tile * n_items + k, so all items of a
 // tile run before the next tile starts: the gathered slab R_{t-1} x tile stays resident in L2.
 //
 // Load balance.  Inside a CTA the item's rows and edges are split evenly over the 8 warps by the
@@ -13,19 +13,31 @@
 // per warp in shared memory; after a barrier one warp sums them in warp order and finishes the row,
 // so results are bitwise reproducible and independent of the batch width.
 //
-// Gather.  A half-warp covers the tile with one 16-byte load per lane per edge; the two half-warps
-// take alternate edges of the same row and are summed with one xor-shuffle at the row end.  Column
-// indices and values are loaded 32 edges at a time, coalesced, and broadcast with shuffles.
+// Gather.  kLanesPerEdge lanes cover the tile with one 16-byte load each per edge; the 32 / kLanesPerEdge
+// lane groups of a warp take interleaved edges of the same row and are summed with xor-shuffles at the
+// row end.  Column indices and values are loaded 32 edges at a time, coalesced, and broadcast with
+// shuffles.
 // Accumulation is float32 in every mode.
 #include "internal.cuh"
 
 namespace afb {
 namespace {
 
-constexpr int kWarps = 8;
-constexpr int kLanesPerEdge = 16;
-constexpr int kUnroll = 4;
+#ifndef AFB_WARPS
+#define AFB_WARPS 8
+#endif
+#ifndef AFB_UNROLL
+#define AFB_UNROLL 4
+#endif
+#ifndef AFB_MINBLOCKS
+#define AFB_MINBLOCKS 1
+#endif
+constexpr int kWarps = AFB_WARPS;              // warps per CTA
+constexpr int kLanesPerEdge = AFB_LPE;         // lanes that cover one gathered row tile (16 bytes each)
+constexpr int kGroups = 32 / kLanesPerEdge;    // edges a warp gathers side by side
+constexpr int kUnroll = AFB_UNROLL;            // gathers in flight per lane
 constexpr unsigned kFull = 0xffffffffu;
+static_assert(kLanesPerEdge == 8 || kLanesPerEdge == 16 || kLanesPerEdge == 32, "lanes per edge");
 
 template <typename T>
 struct Lane;  // 16 bytes of state per lane
@@ -70,9 +82,12 @@ __device__ __forceinline__ float to_f(float v) { return v; }
 __device__ __forceinline__ float to_f(__half v) { return __half2float(v); }
 
 // Finish one row: epilogue of the state update, writes V columns of this lane.
-template <typename T>
-__device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t col0, float (&acc)[Lane<T>::V]) {
+// State buffers are tile-major: element (row, column c) of a step's state lives at
+// tile * ts + row * BT + (c % BT) with tile = c / BT, so one tile's slab is contiguous.
+template <typename T, int BT>
+__device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t tile, int off, float (&acc)[Lane<T>::V]) {
     constexpr int V = Lane<T>::V;
+    const int64_t col0 = tile * BT + off;          // batch column of this lane's first element
     const int4 w0 = __ldg(reinterpret_cast<const int4 *>(a.rc + row));
     const int4 w1 = __ldg(reinterpret_cast<const int4 *>(a.rc + row) + 1);
     const float kk = __int_as_float(w0.x), lo = __int_as_float(w0.y), hi = __int_as_float(w0.z), e = __int_as_float(w0.w);
@@ -96,7 +111,7 @@ __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t c
     }
     float p[V];
     if (prev >= 0) {
-        Lane<T>::load(static_cast<const T *>(a.x_in) + (int64_t)prev * a.ld_in + col0, p);
+        Lane<T>::load(static_cast<const T *>(a.x_in) + tile * a.ts_in + (int64_t)prev * BT + off, p);
     } else {
 #pragma unroll
         for (int k = 0; k < V; ++k) p[k] = pc;
@@ -107,11 +122,11 @@ __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t c
         const float x = fminf(fmaxf(y[k], lo), hi) + e;
         o[k] = p[k] + al * (x - p[k]);
     }
-    Lane<T>::store(static_cast<T *>(a.x_out) + (int64_t)row * a.ld_out + col0, o);
+    Lane<T>::store(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off, o);
 }
 
 template <typename T, typename TV>
-__global__ void __launch_bounds__(kWarps * 32) step_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const StepArgs a) {
     using L = Lane<T>;
     constexpr int V = L::V;
     constexpr int BT = kLanesPerEdge * V;
@@ -123,21 +138,15 @@ __global__ void __launch_bounds__(kWarps * 32) step_kernel(const StepArgs a) {
     const int r0 = __ldg(a.item_rows + item), r1 = __ldg(a.item_rows + item + 1);
     const int e0 = __ldg(a.crow + r0);
     const int nrows = r1 - r0, nnz = __ldg(a.crow + r1) - e0;
-    const int L_ = nrows + nnz;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int grp = lane >> 4, sub = lane & 15;
-    const int64_t col0 = tile * BT + sub * V;
+    const int grp = lane / kLanesPerEdge, sub = lane % kLanesPerEdge;
+    const int off = sub * V;
+    const T *x_tile = static_cast<const T *>(a.x_in) + tile * a.ts_in + off;
 
-    if (tid <= kWarps) {  // merge-path coordinates of the warp boundaries
-        const int d = (int)(((int64_t)L_ * tid) / kWarps);
-        int lo = d - nnz > 0 ? d - nnz : 0, hi = d < nrows ? d : nrows;
-        while (lo < hi) {
-            const int mid = (lo + hi) >> 1;
-            if (__ldg(a.crow + r0 + mid + 1) - e0 <= d - mid - 1) lo = mid + 1;
-            else hi = mid;
-        }
-        s_bi[tid] = lo;
-        s_bj[tid] = d - lo;
+    if (tid <= kWarps) {  // merge-path coordinates of the warp boundaries (precomputed per item)
+        const int2 bd = __ldg(a.bounds + item * (kWarps + 1) + tid);
+        s_bi[tid] = bd.x;
+        s_bj[tid] = bd.y;
     }
     for (int k = tid; k < kWarps * BT; k += kWarps * 32) (&s_first[0][0])[k] = (&s_last[0][0])[k] = 0.f;
     __syncthreads();
@@ -152,7 +161,6 @@ __global__ void __launch_bounds__(kWarps * 32) step_kernel(const StepArgs a) {
     };
 
     const TV *val = static_cast<const TV *>(a.val);
-    const T *x_in = static_cast<const T *>(a.x_in);
     const int is = s_bi[warp], js = s_bj[warp], ie = s_bi[warp + 1], je = s_bj[warp + 1];
     const bool cut_lo = cut(warp), cut_hi = cut(warp + 1);
     for (int i = is; i <= ie && i < nrows; ++i) {
@@ -171,16 +179,16 @@ __global__ void __launch_bounds__(kWarps * 32) step_kernel(const StepArgs a) {
                 my_col = __ldg(a.col + e0 + base + lane);
                 my_val = to_f(val[e0 + base + lane]);
             }
-            for (int k = 0; k < n; k += 2 * kUnroll) {
+            for (int k = 0; k < n; k += kGroups * kUnroll) {
                 float x[kUnroll][V];
                 float v[kUnroll];
 #pragma unroll
                 for (int u = 0; u < kUnroll; ++u) {
-                    const int kk = k + 2 * u + grp;
+                    const int kk = k + kGroups * u + grp;
                     const int c = __shfl_sync(kFull, my_col, kk & 31);
                     v[u] = __shfl_sync(kFull, my_val, kk & 31);
                     if (kk < n) {
-                        L::load(x_in + (int64_t)c * a.ld_in + col0, x[u]);
+                        L::load(x_tile + (int64_t)c * BT, x[u]);
                     } else {
                         v[u] = 0.f;
 #pragma unroll
@@ -194,7 +202,9 @@ __global__ void __launch_bounds__(kWarps * 32) step_kernel(const StepArgs a) {
             }
         }
 #pragma unroll
-        for (int q = 0; q < V; ++q) acc[q] += __shfl_xor_sync(kFull, acc[q], 16);
+        for (int off = kLanesPerEdge; off < 32; off <<= 1)
+#pragma unroll
+            for (int q = 0; q < V; ++q) acc[q] += __shfl_xor_sync(kFull, acc[q], off);
         const bool span_lo = (i == is) && cut_lo, span_hi = (i == ie) && cut_hi;
         if (span_lo || span_hi) {
             // a cut row: its first partial goes to s_first of every warp that starts inside it, the
@@ -205,7 +215,7 @@ __global__ void __launch_bounds__(kWarps * 32) step_kernel(const StepArgs a) {
                 for (int q = 0; q < V; ++q) slot[sub * V + q] = acc[q];
             }
         } else if (i < ie && grp == 0) {
-            finish_row<T>(a, r0 + i, col0, acc);
+            finish_row<T, BT>(a, r0 + i, tile, off, acc);
         }
     }
     __syncthreads();
@@ -221,12 +231,12 @@ __global__ void __launch_bounds__(kWarps * 32) step_kernel(const StepArgs a) {
             for (int q = 0; q < V; ++q) acc[q] += s_first[w][sub * V + q];
             if (!(w + 1 < kWarps && s_bi[w + 1] == row && cut(w + 1))) break;
         }
-        finish_row<T>(a, r0 + row, col0, acc);
+        finish_row<T, BT>(a, r0 + row, tile, off, acc);
     }
 }
 
 __global__ void output_kernel(int n_out, const int *__restrict__ src, const float *__restrict__ base, int add_base,
-                              const void *__restrict__ state, int is_half, int64_t ld_state, float *__restrict__ out,
+                              const void *__restrict__ state, int is_half, int bt, int64_t ts, float *__restrict__ out,
                               int64_t ld_out, int64_t batch) {
     for (int o = blockIdx.x; o < n_out; o += gridDim.x) {
         const int s = src ? src[o] : (state ? o : -1);   // no map: copy row for row, or fill
@@ -234,8 +244,9 @@ __global__ void output_kernel(int n_out, const int *__restrict__ src, const floa
         for (int64_t c = threadIdx.x; c < batch; c += blockDim.x) {
             float v = b0;
             if (s >= 0) {
-                const float x = is_half ? __half2float(static_cast<const __half *>(state)[(int64_t)s * ld_state + c])
-                                        : static_cast<const float *>(state)[(int64_t)s * ld_state + c];
+                const int64_t at = (c / bt) * ts + (int64_t)s * bt + c % bt;
+                const float x = is_half ? __half2float(static_cast<const __half *>(state)[at])
+                                        : static_cast<const float *>(state)[at];
                 v = add_base ? b0 + x : x;
             }
             out[(int64_t)o * ld_out + c] = v;
@@ -255,28 +266,420 @@ __global__ void spmv_kernel(int n_rows, const int *__restrict__ crow, const int 
     }
 }
 
+// ---- pipelined variant: gathers land in shared memory through cp.async ------------------------
+// Each warp owns one edge range (merge path, as above) and a private ring of kStages stages of kChunk
+// edges.  A whole warp covers one edge's row tile (32 lanes x 16 bytes: 256 half or 128 float
+// columns); lane l copies and later reads back only its own 16 bytes, so per-thread cp.async
+// wait_group ordering is all the ring needs.  Bytes in flight live in shared memory, not registers:
+// (kStages - 1) x kChunk x 512 bytes per warp.  A chunk that lies inside one row takes the branch-free
+// path; chunks that cross a row end go edge by edge.  The product of two float16 values is exact in
+// float32, so the mixed-precision fma.rn.f32.f16 (float16 inputs, float32 accumulator, one rounding)
+// gives the same sums as converting first, at half the instructions; float32 state uses the packed
+// fma.rn.f32x2.  Row constants of the warp's next 32 rows are staged in shared memory.
+#ifndef AFB_STAGES
+#define AFB_STAGES 3
+#endif
+#ifndef AFB_CHUNK
+#define AFB_CHUNK 4
+#endif
+#ifndef AFB_ASYNC_WARPS
+#define AFB_ASYNC_WARPS 8
+#endif
+#ifndef AFB_ASYNC_MINBLOCKS
+#define AFB_ASYNC_MINBLOCKS 3
+#endif
+constexpr int kAWarps = AFB_ASYNC_WARPS;
+constexpr int kStages = AFB_STAGES;
+constexpr int kChunk = AFB_CHUNK;
+constexpr int kRowBytes = 512;
+constexpr int kWarpRing = kStages * kChunk * kRowBytes;
+constexpr int kRingBytes = kAWarps * kWarpRing;
+static_assert(32 % kChunk == 0, "a chunk must not straddle a 32-edge window");
+static_assert(kWarpRing >= 256 * 4, "a warp's ring must hold its cut-row partial after the main loop");
+
+#ifndef AFB_CP_CG
+#define AFB_CP_CG 0
+#endif
+// Through L1 (.ca) a warp's 32 x 16 contiguous bytes coalesce into four 128-byte requests; the L2-only
+// form (.cg) was measured to move twice the gathered bytes from L2.
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    if (AFB_CP_CG) asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+    else asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+// L2 eviction priorities: the gathered slab of a tile is read ~60 times while the tile is processed,
+// everything else (sub-matrix indices and values, the input drive, the new state) once.  Marking the
+// one-pass traffic evict-first and the slab evict-last keeps the slab resident in L2.
+#ifndef AFB_L2HINT
+#define AFB_L2HINT 1
+#endif
+__device__ __forceinline__ uint64_t policy_keep() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ uint64_t policy_stream() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
+    return p;
+}
+__device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void *src, uint64_t pol) {
+    if (!AFB_L2HINT) return cp_async16(dst, src);
+    asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "l"(pol) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_stream_b32(const void *p, uint64_t pol) {
+    uint32_t v;
+    if (AFB_L2HINT) asm volatile("ld.global.nc.L2::cache_hint.b32 %0, [%1], %2;\n" : "=r"(v) : "l"(p), "l"(pol));
+    else v = __ldg(static_cast<const unsigned *>(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ld_stream_b16(const void *p, uint64_t pol) {
+    unsigned short v;
+    if (AFB_L2HINT) asm volatile("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;\n" : "=h"(v) : "l"(p), "l"(pol));
+    else v = __ldg(static_cast<const unsigned short *>(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ld_stream_v4(const void *p, uint64_t pol) {
+    uint4 v;
+    if (AFB_L2HINT)
+        asm volatile("ld.global.nc.L2::cache_hint.v4.b32 {%0, %1, %2, %3}, [%4], %5;\n"
+                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p), "l"(pol));
+    else v = __ldg(static_cast<const uint4 *>(p));
+    return v;
+}
+__device__ __forceinline__ void st_stream_v4(void *p, uint4 v, uint64_t pol) {
+    if (AFB_L2HINT)
+        asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;\n" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                     "r"(v.w), "l"(pol) : "memory");
+    else *static_cast<uint4 *>(p) = v;
+}
+
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
+
+template <typename T>
+struct Gather;
+
+template <>
+struct Gather<__half> {
+    static constexpr int V = 8;
+    __device__ static uint32_t bits(const __half *p, uint64_t pol) { return ld_stream_b16(p, pol); }
+    // acc[0..7] += v * x[0..7], x = the 8 float16 values at shared address addr
+    __device__ static void fma(float (&acc)[8], uint32_t v, uint32_t addr) {
+        uint32_t r[4];
+        asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+        const unsigned short vh = (unsigned short)v;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            unsigned short lo, hi;
+            asm("mov.b32 {%0, %1}, %2;\n" : "=h"(lo), "=h"(hi) : "r"(r[k]));
+            asm("fma.rn.f32.f16 %0, %1, %2, %0;\n" : "+f"(acc[2 * k]) : "h"(lo), "h"(vh));
+            asm("fma.rn.f32.f16 %0, %1, %2, %0;\n" : "+f"(acc[2 * k + 1]) : "h"(hi), "h"(vh));
+        }
+    }
+};
+
+template <>
+struct Gather<float> {
+    static constexpr int V = 4;
+    __device__ static uint32_t bits(const float *p, uint64_t pol) { return ld_stream_b32(p, pol); }
+    __device__ static void fma(float (&acc)[4], uint32_t v, uint32_t addr) {
+        float x[4];
+        asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];\n" : "=f"(x[0]), "=f"(x[1]), "=f"(x[2]), "=f"(x[3]) : "r"(addr));
+        const float vf = __uint_as_float(v);
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+            asm("{\n .reg .b64 a, x, v;\n mov.b64 a, {%0, %1};\n mov.b64 x, {%2, %3};\n mov.b64 v, {%4, %4};\n"
+                " fma.rn.f32x2 a, x, v, a;\n mov.b64 {%0, %1}, a;\n}\n"
+                : "+f"(acc[2 * k]), "+f"(acc[2 * k + 1]) : "f"(x[2 * k]), "f"(x[2 * k + 1]), "f"(vf));
+    }
+};
+
+// finish_row with the row's constants already at hand (shared memory)
+template <typename T>
+__device__ __forceinline__ void load_stream(const T *p, float (&x)[Lane<T>::V], uint64_t pol) {
+    const uint4 v = ld_stream_v4(p, pol);
+    if constexpr (sizeof(T) == 4) {
+        x[0] = __uint_as_float(v.x); x[1] = __uint_as_float(v.y); x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
+    } else {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(h[k]);
+            x[2 * k] = f.x;
+            x[2 * k + 1] = f.y;
+        }
+    }
+}
+template <typename T>
+__device__ __forceinline__ void store_stream(T *p, const float (&x)[Lane<T>::V], uint64_t pol) {
+    uint4 v;
+    if constexpr (sizeof(T) == 4) {
+        v = make_uint4(__float_as_uint(x[0]), __float_as_uint(x[1]), __float_as_uint(x[2]), __float_as_uint(x[3]));
+    } else {
+        __half2 *h = reinterpret_cast<__half2 *>(&v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) h[k] = __floats2half2_rn(x[2 * k], x[2 * k + 1]);
+    }
+    st_stream_v4(p, v, pol);
+}
+
+template <typename T, int BT>
+__device__ __forceinline__ void finish_row_q(const StepArgs &a, const RowConst *q_s, int row, int64_t tile, int off,
+                                             float (&acc)[Lane<T>::V], uint64_t pol) {
+    constexpr int V = Lane<T>::V;
+    const int4 w0 = reinterpret_cast<const int4 *>(q_s)[0];
+    const int4 w1 = reinterpret_cast<const int4 *>(q_s)[1];
+    const float kk = __int_as_float(w0.x), lo = __int_as_float(w0.y), hi = __int_as_float(w0.z), e = __int_as_float(w0.w);
+    const float pc = __int_as_float(w1.x), al = __int_as_float(w1.y);
+    const int prev = w1.z, usrc = w1.w;
+    const int64_t col0 = tile * BT + off;
+    float p[V], ux[V];
+    if (prev >= 0) Lane<T>::load(static_cast<const T *>(a.x_in) + tile * a.ts_in + (int64_t)prev * BT + off, p);
+    if (usrc >= 0) {
+        const T *u = static_cast<const T *>(a.u) + (int64_t)usrc * a.ld_u + col0;
+        if (a.u_vec_ok && col0 + V <= a.batch) {
+            load_stream<T>(u, ux, pol);
+        } else {
+#pragma unroll
+            for (int k = 0; k < V; ++k) ux[k] = col0 + k < a.batch ? Lane<T>::scalar(u + k) : 0.f;
+        }
+    }
+    float o[V];
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+        const float y = acc[k] + kk + (usrc >= 0 ? ux[k] : 0.f);
+        const float x = fminf(fmaxf(y, lo), hi) + e;
+        const float pk = prev >= 0 ? p[k] : pc;
+        o[k] = pk + al * (x - pk);
+    }
+    store_stream<T>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off, o, pol);
+}
+
+template <typename T, typename TV>
+__global__ void __launch_bounds__(kAWarps * 32, AFB_ASYNC_MINBLOCKS) step_kernel_async(const StepArgs a) {
+    using G = Gather<T>;
+    constexpr int V = G::V;
+    constexpr int BT = 32 * V;
+    extern __shared__ __align__(16) unsigned char ring[];
+    __shared__ float s_first[kAWarps][BT];
+    __shared__ __align__(16) RowConst s_rc[kAWarps][32];
+    __shared__ int s_bi[kAWarps + 1], s_bj[kAWarps + 1];
+
+    const int item = __ldg(a.item_order + (blockIdx.x % a.n_items));
+    const int64_t tile = blockIdx.x / a.n_items;
+    const int r0 = __ldg(a.item_rows + item), r1 = __ldg(a.item_rows + item + 1);
+    const int e0 = __ldg(a.crow + r0);
+    const int nrows = r1 - r0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int off = lane * V;
+    if (tid <= kAWarps) {
+        const int2 bd = __ldg(a.bounds + item * (kAWarps + 1) + tid);
+        s_bi[tid] = bd.x;
+        s_bj[tid] = bd.y;
+    }
+    for (int k = tid; k < kAWarps * BT; k += kAWarps * 32) (&s_first[0][0])[k] = 0.f;
+    __syncthreads();
+    auto cut = [&](int b) -> bool { return b >= 1 && b < kAWarps && s_bj[b] > __ldg(a.crow + r0 + s_bi[b]) - e0; };
+    auto first_cut = [&](int b) -> int {
+        while (b > 1 && s_bi[b - 1] == s_bi[b] && cut(b - 1)) --b;
+        return b;
+    };
+
+    const int is = s_bi[warp], js = s_bj[warp], ie = s_bi[warp + 1], je = s_bj[warp + 1];
+    const bool cut_lo = cut(warp), cut_hi = cut(warp + 1);
+    const T *x_tile = static_cast<const T *>(a.x_in) + tile * a.ts_in + off;
+    const int *colp = a.col + e0;
+    const TV *valp = static_cast<const TV *>(a.val) + e0;
+    const uint32_t ring_warp = (uint32_t)__cvta_generic_to_shared(ring) + warp * kWarpRing + lane * 16;
+    const uint64_t keep = policy_keep(), stream = policy_stream();
+
+    // row constants of rows rcb .. rcb + 31 (relative to r0), one per lane, in shared memory
+    int rcb = is;
+    auto load_rc = [&](int base) {
+        rcb = base;
+        const int r = base + lane;
+        if (r < nrows) {
+            const int4 *src = reinterpret_cast<const int4 *>(a.rc + r0 + r);
+            int4 *dst = reinterpret_cast<int4 *>(&s_rc[warp][lane]);
+            dst[0] = __ldg(src);
+            dst[1] = __ldg(src + 1);
+        }
+        __syncwarp();
+    };
+    load_rc(is);
+
+    const int n_chunks = (je - js + kChunk - 1) / kChunk;
+    int pcol = 0;
+    auto prefetch = [&](int k) {      // chunk k -> stage k % kStages
+        if (k < n_chunks) {
+            const int cs = js + k * kChunk, wo = (k * kChunk) & 31;
+            if (wo == 0) pcol = cs + lane < je ? (int)ld_stream_b32(colp + cs + lane, stream) : 0;
+            const uint32_t dst = ring_warp + (k % kStages) * (kChunk * kRowBytes);
+            if (cs + kChunk <= je) {
+#pragma unroll
+                for (int u = 0; u < kChunk; ++u) {
+                    const int c = __shfl_sync(kFull, pcol, wo + u);
+                    cp_async16_hint(dst + u * kRowBytes, x_tile + c * BT, keep);
+                }
+            } else {
+#pragma unroll
+                for (int u = 0; u < kChunk; ++u) {
+                    const int c = __shfl_sync(kFull, pcol, wo + u);
+                    if (cs + u < je) cp_async16_hint(dst + u * kRowBytes, x_tile + c * BT, keep);
+                }
+            }
+        }
+        cp_async_commit();
+    };
+#pragma unroll
+    for (int st = 0; st < kStages - 1; ++st) prefetch(st);
+
+    int rend_base = -64, rend = 0;    // ends (relative edge index) of rows rend_base .. +31
+    auto row_end = [&](int i) -> int {
+        if (i >= rend_base + 32 || i < rend_base) {
+            rend_base = i;
+            rend = i + lane < nrows ? __ldg(a.crow + r0 + i + lane + 1) - e0 : 0x7fffffff;
+        }
+        return __shfl_sync(kFull, rend, i - rend_base);
+    };
+    int cur = is;
+    int cur_end = cur < nrows ? row_end(cur) : 0x7fffffff;
+    float acc[V];
+#pragma unroll
+    for (int q = 0; q < V; ++q) acc[q] = 0.f;
+    auto close_row = [&](int i) {     // all of row i's edges in this warp are summed and its end is in range
+        if (i == is && cut_lo) {
+#pragma unroll
+            for (int q = 0; q < V; ++q) s_first[warp][off + q] = acc[q];
+        } else {
+            if (i - rcb >= 32) load_rc(i);
+            finish_row_q<T, BT>(a, &s_rc[warp][i - rcb], r0 + i, tile, off, acc, stream);
+        }
+#pragma unroll
+        for (int q = 0; q < V; ++q) acc[q] = 0.f;
+    };
+
+    uint32_t vwin = 0;
+    for (int k = 0; k < n_chunks; ++k) {
+        prefetch(k + kStages - 1);
+        cp_async_wait<kStages - 1>();
+        const int cs = js + k * kChunk, wo = (k * kChunk) & 31;
+        if (wo == 0) vwin = cs + lane < je ? G::bits(valp + cs + lane, stream) : 0u;
+        const uint32_t src = ring_warp + (k % kStages) * (kChunk * kRowBytes);
+        if (cs + kChunk <= cur_end && cs + kChunk <= je) {
+#pragma unroll
+            for (int u = 0; u < kChunk; ++u) G::fma(acc, __shfl_sync(kFull, vwin, wo + u), src + u * kRowBytes);
+        } else {
+#pragma unroll
+            for (int u = 0; u < kChunk; ++u) {
+                const int e = cs + u;
+                if (e < je) {
+                    while (e >= cur_end) {
+                        close_row(cur);
+                        ++cur;
+                        cur_end = row_end(cur);
+                    }
+                    G::fma(acc, __shfl_sync(kFull, vwin, wo + u), src + u * kRowBytes);
+                }
+            }
+        }
+    }
+    cp_async_wait<0>();
+    while (cur < ie) {
+        close_row(cur);
+        ++cur;
+    }
+    float *s_last_w = reinterpret_cast<float *>(ring + warp * kWarpRing);   // the ring is idle from here on
+    if (cut_hi) {
+        float *slot = (ie == is && cut_lo) ? s_first[warp] : s_last_w;
+#pragma unroll
+        for (int q = 0; q < V; ++q) slot[off + q] = acc[q];
+    }
+    __syncthreads();
+    const int b = warp + 1;
+    if (b < kAWarps && cut(b) && first_cut(b) == b) {
+        const int row = s_bi[b];
+        const float *s_last_p = reinterpret_cast<const float *>(ring + (b - 1) * kWarpRing);
+        float sum[V];
+#pragma unroll
+        for (int q = 0; q < V; ++q) sum[q] = s_last_p[off + q];
+        for (int w = b;; ++w) {
+#pragma unroll
+            for (int q = 0; q < V; ++q) sum[q] += s_first[w][off + q];
+            if (!(w + 1 < kAWarps && s_bi[w + 1] == row && cut(w + 1))) break;
+        }
+        finish_row<T, BT>(a, r0 + row, tile, off, sum);
+    }
+}
+
+#ifndef AFB_ASYNC
+#define AFB_ASYNC 1
+#endif
+
 template <typename T, typename TV>
 void launch(const StepArgs &a, cudaStream_t s) {
-    constexpr int BT = kLanesPerEdge * Lane<T>::V;
+    constexpr int BT = (AFB_ASYNC ? 32 : kLanesPerEdge) * Lane<T>::V;
     if (a.n_items == 0 || a.batch == 0) return;
     const int64_t tiles = (a.batch + BT - 1) / BT;
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
-    step_kernel<T, TV><<<(unsigned)blocks, kWarps * 32, 0, s>>>(a);
+    if (AFB_ASYNC) {
+        static unsigned long long configured = 0;   // devices on which this instantiation may use kRingBytes
+        int dev = 0;
+        AFB_CUDA(cudaGetDevice(&dev));
+        if (dev < 64 && !(configured >> dev & 1ull)) {
+            AFB_CUDA(cudaFuncSetAttribute(step_kernel_async<T, TV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kRingBytes));
+            configured |= 1ull << dev;
+        }
+        step_kernel_async<T, TV><<<(unsigned)blocks, kAWarps * 32, kRingBytes, s>>>(a);
+    } else {
+        step_kernel<T, TV><<<(unsigned)blocks, kWarps * 32, 0, s>>>(a);
+    }
     AFB_LAUNCHED();
 }
 
 }  // namespace
 
 void launch_step_f32(const StepArgs &a, cudaStream_t s) { launch<float, float>(a, s); }
+__global__ void bounds_kernel(int n_items, int warps, const int *__restrict__ crow, const int *__restrict__ item_rows,
+                              int2 *__restrict__ bounds) {
+    for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < (int64_t)n_items * (warps + 1);
+         k += (int64_t)gridDim.x * blockDim.x) {
+        const int item = (int)(k / (warps + 1)), b = (int)(k % (warps + 1));
+        const int r0 = item_rows[item], r1 = item_rows[item + 1];
+        const int e0 = crow[r0], nrows = r1 - r0, nnz = crow[r1] - e0;
+        const int d = (int)(((int64_t)(nrows + nnz) * b) / warps);
+        int lo = d - nnz > 0 ? d - nnz : 0, hi = d < nrows ? d : nrows;
+        while (lo < hi) {                      // merge path: row ends consumed at diagonal d
+            const int mid = (lo + hi) >> 1;
+            if (crow[r0 + mid + 1] - e0 <= d - mid - 1) lo = mid + 1;
+            else hi = mid;
+        }
+        bounds[k] = make_int2(lo, d - lo);
+    }
+}
+
+int tile_cols(int elem_bytes) { return (AFB_ASYNC ? 32 : kLanesPerEdge) * (16 / elem_bytes); }
 void launch_step_dev16(const StepArgs &a, cudaStream_t s) { launch<__half, __half>(a, s); }
 
+void build_bounds(Csr &m, cudaStream_t s) {
+    const int warps = AFB_ASYNC ? kAWarps : kWarps;
+    m.bounds.alloc((size_t)m.n_items * (warps + 1));
+    if (m.n_items) {
+        bounds_kernel<<<grid_for((int64_t)m.n_items * (warps + 1), 256), 256, 0, s>>>(m.n_items, warps, m.crow.get(),
+                                                                                       m.item_rows.get(), m.bounds.get());
+        AFB_LAUNCHED();
+    }
+}
+
 void launch_output(int n_out, const int *src, const float *base, int add_base, const void *state, int state_is_half,
-                   int64_t ld_state, float *out, int64_t ld_out, int64_t batch, cudaStream_t s) {
+                   int64_t ts_state, float *out, int64_t ld_out, int64_t batch, cudaStream_t s) {
+    const int bt = tile_cols(state_is_half ? 2 : 4);
     if (n_out == 0 || batch == 0) return;
     const int threads = 256;
     const int grid = n_out < 148 * 64 ? n_out : 148 * 64;
-    output_kernel<<<grid, threads, 0, s>>>(n_out, src, base, add_base, state, state_is_half, ld_state, out, ld_out, batch);
+    output_kernel<<<grid, threads, 0, s>>>(n_out, src, base, add_base, state, state_is_half, bt, ts_state, out, ld_out, batch);
     AFB_LAUNCHED();
 }
 

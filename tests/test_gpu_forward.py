@@ -228,7 +228,7 @@ def test_strided_input_and_weight_updates_invalidate_the_cache(small):
         rnn.bias.sub_(0.05)
         d = rnn.forward_io(u, inst.in_idx.to(DEV), inst.out_idx.to(DEV), 6)
     assert not torch.allclose(a, c)
-    torch.testing.assert_close(a, d, rtol=1e-6, atol=1e-6)
+    torch.testing.assert_close(a, d, rtol=1e-5, atol=1e-5)         # b + 0.05 - 0.05 is not exact in float32
 
 
 def test_columns_are_independent_at_full_batch(full):
