@@ -178,6 +178,14 @@ class LightCone:
                                                       _stream(self.device)))
         self._weights[mode] = key
 
+    def status(self, reset: bool = True) -> int:
+        """Device status word of this cone's step kernels: 0 = ok, 1 = a bounded wait gave up (some
+        forward since the last reset produced invalid output).  Synchronises the current stream."""
+        st = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.afb_cone_status(self._h, ctypes.byref(st), int(reset), _stream(self.device)))
+        return st.value
+
     def forward(self, mode: int, u_in: torch.Tensor, events=None) -> torch.Tensor:
         """Native forward; ``events`` (steps + 2 recorded torch.cuda.Event objects with timing) brackets
         each step's kernel and the output kernel for per-step timing."""
@@ -216,6 +224,12 @@ class _Graph:
                 pass
             self._lib.afb_graph_destroy(h)
             self._h = None
+
+    def status(self, reset: bool = True) -> int:
+        st = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.afb_graph_status(self._h, ctypes.byref(st), int(reset), _stream(self.device)))
+        return st.value
 
     def forward(self, rnn: "ConnectomeRNN", u: torch.Tensor, steps: int) -> torch.Tensor:
         batch = u.shape[1]
@@ -306,6 +320,15 @@ class ConnectomeRNN(nn.Module):
             raise TypeError(f"alphafly_b200 computes in float32 or float16, got {u.dtype}")
         h = self._graph().forward(self, u.float().contiguous(), steps)
         return h.to(u.dtype)
+
+    def device_status(self, reset: bool = True) -> int:
+        """0 if every native kernel since the last reset completed normally, else the library's status
+        code (see ``afb_cone_status``).  Synchronises the device's current stream."""
+        st = 0
+        for cache in (getattr(self, "_cone", None), getattr(self, "_graph_cache", None)):
+            if cache is not None:
+                st = st or cache[1].status(reset)
+        return st
 
     # -- the same function through the light cone ---------------------------------------------------
     def light_cone(self, in_idx: torch.Tensor, out_idx: torch.Tensor, steps: int) -> LightCone:

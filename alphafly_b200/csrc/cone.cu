@@ -342,12 +342,34 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
             if (c->n_hit) gather_int<<<grid_for(c->n_hit, kBlock), kBlock, 0, s>>>(c->out_row.get(), c->out_pos.get(), c->out_src.get(), c->n_hit);
             AFB_LAUNCHED();
         }
+        c->err.alloc(1);
+        AFB_CUDA(cudaMemsetAsync(c->err.get(), 0, sizeof(int), s));
         AFB_CUDA(cudaStreamSynchronize(s));
         *out = c.release();
     });
 }
 
 void afb_cone_destroy(afb_cone *cone) { delete cone; }
+
+static int read_status(int *word, int *status, int reset, void *stream) {
+    return guarded([&] {
+        AFB_CHECK(word && status, "NULL pointer");
+        cudaStream_t s = as_stream(stream);
+        AFB_CUDA(cudaMemcpyAsync(status, word, sizeof(int), cudaMemcpyDeviceToHost, s));
+        if (reset) AFB_CUDA(cudaMemsetAsync(word, 0, sizeof(int), s));
+        AFB_CUDA(cudaStreamSynchronize(s));
+    });
+}
+
+int afb_cone_status(const afb_cone *c, int *status, int reset, void *stream) {
+    if (!c) { set_last_error("cone is NULL"); return AFB_EINVAL; }
+    return read_status(c->err.get(), status, reset, stream);
+}
+
+int afb_graph_status(const afb_graph *g, int *status, int reset, void *stream) {
+    if (!g) { set_last_error("graph is NULL"); return AFB_EINVAL; }
+    return read_status(g->err.get(), status, reset, stream);
+}
 
 int afb_cone_sizes(const afb_cone *c, int64_t *rows_len, int64_t *nnz, int64_t *n_keep, int64_t *n_fed,
                    int64_t *n_hit, int64_t *edge_visits) {
@@ -438,6 +460,8 @@ int afb_graph_create(afb_graph **out, int64_t n, int64_t e, const int64_t *pre, 
         AFB_CUDA(cudaMemsetAsync(g->empty.crow.get(), 0, (n + 1) * sizeof(int), s));
         g->empty.col.alloc(1);
         build_schedule(g->empty, s);
+        g->err.alloc(1);
+        AFB_CUDA(cudaMemsetAsync(g->err.get(), 0, sizeof(int), s));
         AFB_CUDA(cudaStreamSynchronize(s));
         *out = g.release();
     });

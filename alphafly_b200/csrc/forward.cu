@@ -246,6 +246,7 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
             a.x_out = buf[t & 1];
             a.ts_out = (int64_t)sp.n_rows * bt;
             a.batch = batch;
+            a.err = c->err.get();
             if (events) AFB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[t - 1]), s));
             if (mode == AFB_MODE_F32) launch_step_f32(a, s);
             else launch_step_dev16(a, s);
@@ -316,6 +317,7 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
             a.x_out = buf[t & 1];
             a.ts_out = ts;
             a.batch = batch;
+            a.err = g->err.get();
             launch_step_f32(a, s);
             x_in = buf[t & 1];
         }

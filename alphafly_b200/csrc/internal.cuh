@@ -80,6 +80,7 @@ struct StepArgs {
     void *x_out;                   // state of R_t, tile-major
     int64_t ts_out;
     int64_t batch;
+    int *err;                      // device status word: set non-zero when a bounded wait gives up
 };
 
 // Batch columns one CTA covers for a state element of `elem_bytes`; the state's leading dimension is
@@ -122,10 +123,12 @@ struct afb_cone {
     afb::DevBuf<float> wc;             // (n) scratch of the resting-trajectory SpMV
     afb::DevBuf<float> out_base[2];    // c_T[out_idx], per mode
     bool ready[2] = {false, false};    // per mode: constants set since the handle was built
+    afb::DevBuf<int> err;              // device status word of the step kernels (0 = ok)
 };
 
 struct afb_graph {
     int64_t n = 0, e = 0;
     afb::Csr full;                     // W over all neurons (edge order = CSR order)
     afb::Csr empty;                    // no entries: the first step multiplies a zero state
+    afb::DevBuf<int> err;              // device status word of the step kernels (0 = ok)
 };

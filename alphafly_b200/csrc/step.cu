@@ -424,9 +424,43 @@ __device__ __forceinline__ void store_stream(T *p, const float (&x)[Lane<T>::V],
     st_stream_v4(p, v, pol);
 }
 
+// The epilogue inputs of a row (its previous state and its input drive, 16 raw bytes per lane), loaded
+// one row ahead so that the loads are in flight while the row's edges are summed.
+struct RowPre {
+    uint4 p, u;
+};
+
+template <typename T>
+__device__ __forceinline__ void raw_to_floats(const uint4 &v, float (&x)[Lane<T>::V]) {
+    if constexpr (sizeof(T) == 4) {
+        x[0] = __uint_as_float(v.x); x[1] = __uint_as_float(v.y); x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
+    } else {
+        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(h[k]);
+            x[2 * k] = f.x;
+            x[2 * k + 1] = f.y;
+        }
+    }
+}
+
 template <typename T, int BT>
-__device__ __forceinline__ void finish_row_q(const StepArgs &a, const RowConst *q_s, int row, int64_t tile, int off,
-                                             float (&acc)[Lane<T>::V], uint64_t pol) {
+__device__ __forceinline__ RowPre issue_row(const StepArgs &a, const RowConst *q_s, int64_t tile, int off, uint64_t stream) {
+    constexpr int V = Lane<T>::V;
+    RowPre r;
+    const int4 w1 = reinterpret_cast<const int4 *>(q_s)[1];
+    const int prev = w1.z, usrc = w1.w;
+    const int64_t col0 = tile * BT + off;
+    if (prev >= 0) r.p = __ldg(reinterpret_cast<const uint4 *>(static_cast<const T *>(a.x_in) + tile * a.ts_in + (int64_t)prev * BT + off));
+    if (usrc >= 0 && a.u_vec_ok && col0 + V <= a.batch)
+        r.u = ld_stream_v4(static_cast<const T *>(a.u) + (int64_t)usrc * a.ld_u + col0, stream);
+    return r;
+}
+
+template <typename T, int BT>
+__device__ __forceinline__ void finish_row_pre(const StepArgs &a, const RowConst *q_s, const RowPre &pre, int row,
+                                               int64_t tile, int off, float (&acc)[Lane<T>::V], uint64_t stream) {
     constexpr int V = Lane<T>::V;
     const int4 w0 = reinterpret_cast<const int4 *>(q_s)[0];
     const int4 w1 = reinterpret_cast<const int4 *>(q_s)[1];
@@ -435,12 +469,12 @@ __device__ __forceinline__ void finish_row_q(const StepArgs &a, const RowConst *
     const int prev = w1.z, usrc = w1.w;
     const int64_t col0 = tile * BT + off;
     float p[V], ux[V];
-    if (prev >= 0) Lane<T>::load(static_cast<const T *>(a.x_in) + tile * a.ts_in + (int64_t)prev * BT + off, p);
+    if (prev >= 0) raw_to_floats<T>(pre.p, p);
     if (usrc >= 0) {
-        const T *u = static_cast<const T *>(a.u) + (int64_t)usrc * a.ld_u + col0;
         if (a.u_vec_ok && col0 + V <= a.batch) {
-            load_stream<T>(u, ux, pol);
+            raw_to_floats<T>(pre.u, ux);
         } else {
+            const T *u = static_cast<const T *>(a.u) + (int64_t)usrc * a.ld_u + col0;
 #pragma unroll
             for (int k = 0; k < V; ++k) ux[k] = col0 + k < a.batch ? Lane<T>::scalar(u + k) : 0.f;
         }
@@ -453,7 +487,7 @@ __device__ __forceinline__ void finish_row_q(const StepArgs &a, const RowConst *
         const float pk = prev >= 0 ? p[k] : pc;
         o[k] = pk + al * (x - pk);
     }
-    store_stream<T>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off, o, pol);
+    store_stream<T>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off, o, stream);
 }
 
 template <typename T, typename TV>
@@ -508,13 +542,26 @@ __global__ void __launch_bounds__(kAWarps * 32, AFB_ASYNC_MINBLOCKS) step_kernel
         __syncwarp();
     };
     load_rc(is);
+    RowPre pre;
+    auto arm = [&](int i) {           // issue the epilogue loads of row i, the next row this warp finishes
+        if (i < ie) {
+            if (i - rcb >= 32) load_rc(i);
+            pre = issue_row<T, BT>(a, &s_rc[warp][i - rcb], tile, off, stream);
+        }
+    };
+    arm(cut_lo ? is + 1 : is);
 
     const int n_chunks = (je - js + kChunk - 1) / kChunk;
-    int pcol = 0;
+    // 32-edge windows of column indices (for the copies) and values (for the sums), one window ahead
+    int pcol = 0, pcol_nx = js + lane < je ? (int)ld_stream_b32(colp + js + lane, stream) : 0;
+    uint32_t vwin = 0, vwin_nx = js + lane < je ? G::bits(valp + js + lane, stream) : 0u;
     auto prefetch = [&](int k) {      // chunk k -> stage k % kStages
         if (k < n_chunks) {
             const int cs = js + k * kChunk, wo = (k * kChunk) & 31;
-            if (wo == 0) pcol = cs + lane < je ? (int)ld_stream_b32(colp + cs + lane, stream) : 0;
+            if (wo == 0) {
+                pcol = pcol_nx;
+                pcol_nx = cs + 32 + lane < je ? (int)ld_stream_b32(colp + cs + 32 + lane, stream) : 0;
+            }
             const uint32_t dst = ring_warp + (k % kStages) * (kChunk * kRowBytes);
             if (cs + kChunk <= je) {
 #pragma unroll
@@ -553,19 +600,21 @@ __global__ void __launch_bounds__(kAWarps * 32, AFB_ASYNC_MINBLOCKS) step_kernel
 #pragma unroll
             for (int q = 0; q < V; ++q) s_first[warp][off + q] = acc[q];
         } else {
-            if (i - rcb >= 32) load_rc(i);
-            finish_row_q<T, BT>(a, &s_rc[warp][i - rcb], r0 + i, tile, off, acc, stream);
+            finish_row_pre<T, BT>(a, &s_rc[warp][i - rcb], pre, r0 + i, tile, off, acc, stream);
         }
 #pragma unroll
         for (int q = 0; q < V; ++q) acc[q] = 0.f;
+        arm(i + 1);
     };
 
-    uint32_t vwin = 0;
     for (int k = 0; k < n_chunks; ++k) {
         prefetch(k + kStages - 1);
         cp_async_wait<kStages - 1>();
         const int cs = js + k * kChunk, wo = (k * kChunk) & 31;
-        if (wo == 0) vwin = cs + lane < je ? G::bits(valp + cs + lane, stream) : 0u;
+        if (wo == 0) {
+            vwin = vwin_nx;
+            vwin_nx = cs + 32 + lane < je ? G::bits(valp + cs + 32 + lane, stream) : 0u;
+        }
         const uint32_t src = ring_warp + (k % kStages) * (kChunk * kRowBytes);
         if (cs + kChunk <= cur_end && cs + kChunk <= je) {
 #pragma unroll
@@ -613,18 +662,283 @@ __global__ void __launch_bounds__(kAWarps * 32, AFB_ASYNC_MINBLOCKS) step_kernel
     }
 }
 
+// ---- TMA variant: one 512-byte bulk copy per edge, completion on a per-stage mbarrier -----------
+// The same warp-private ring as the cp.async kernel, but the copies run on the TMA path
+// (cp.async.bulk): the gathered bytes no longer pass through the LSU data pipe on their way into
+// shared memory, which measured 85% busy with cp.async.  Lane u < kTChunk issues the copy of the
+// chunk's u-th edge; lane 0 arms the stage's mbarrier with the chunk's byte count.  Every wait is
+// bounded: on timeout the kernel records AFB status 1 in *err and finishes with zeros in place of the
+// lost rows (never observed; it only keeps a lost copy from hanging the GPU).
+#ifndef AFB_TMA
+#define AFB_TMA 0     // measured slower than the cp.async kernel on the configuration-3 workload
+#endif
+#ifndef AFB_TMA_STAGES
+#define AFB_TMA_STAGES 4
+#endif
+#ifndef AFB_TMA_CHUNK
+#define AFB_TMA_CHUNK 4
+#endif
+#ifndef AFB_TMA_MINBLOCKS
+#define AFB_TMA_MINBLOCKS 2
+#endif
+#ifndef AFB_TMA_ONE_LANE
+#define AFB_TMA_ONE_LANE 0
+#endif
+#ifndef AFB_TMA_FENCE
+#define AFB_TMA_FENCE 1
+#endif
+constexpr int kTStages = AFB_TMA_STAGES;
+constexpr int kTChunk = AFB_TMA_CHUNK;
+constexpr int kTWarpRing = kTStages * kTChunk * kRowBytes;
+constexpr int kTRingBytes = kAWarps * kTWarpRing;
+constexpr uint32_t kWaitLimit = 1u << 22;
+constexpr uint32_t kDrainLimit = 1u << 16;
+static_assert(32 % kTChunk == 0 && kTChunk <= 32, "chunk within a 32-edge window");
+static_assert(kTWarpRing >= 256 * 4, "a warp's ring must hold its cut-row partial after the main loop");
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}\n" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+                 : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Polls at most `limit` times; gives up early once any CTA has reported a lost stage in *err.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity, uint32_t limit, const int *err) {
+    for (uint32_t it = 0; it < limit; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 1023u) == 1023u && err && *reinterpret_cast<const volatile int *>(err) != 0) return false;
+    }
+    return false;
+}
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar, uint64_t pol) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n"
+                 ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
+
+template <typename T, typename TV>
+__global__ void __launch_bounds__(kAWarps * 32, AFB_TMA_MINBLOCKS) step_kernel_tma(const StepArgs a) {
+    using G = Gather<T>;
+    constexpr int V = G::V;
+    constexpr int BT = 32 * V;
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ float s_first[kAWarps][BT];
+    __shared__ __align__(16) RowConst s_rc[kAWarps][32];
+    __shared__ __align__(8) uint64_t s_bar[kAWarps][kTStages];
+    __shared__ int s_bi[kAWarps + 1], s_bj[kAWarps + 1];
+
+    const int item = __ldg(a.item_order + (blockIdx.x % a.n_items));
+    const int64_t tile = blockIdx.x / a.n_items;
+    const int r0 = __ldg(a.item_rows + item), r1 = __ldg(a.item_rows + item + 1);
+    const int e0 = __ldg(a.crow + r0);
+    const int nrows = r1 - r0;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int off = lane * V;
+    if (tid <= kAWarps) {
+        const int2 bd = __ldg(a.bounds + item * (kAWarps + 1) + tid);
+        s_bi[tid] = bd.x;
+        s_bj[tid] = bd.y;
+    }
+    if (tid < kAWarps * kTStages) mbar_init((uint32_t)__cvta_generic_to_shared(&s_bar[0][0] + tid), 1);
+    for (int k = tid; k < kAWarps * BT; k += kAWarps * 32) (&s_first[0][0])[k] = 0.f;
+    fence_mbar_init();
+    __syncthreads();
+    auto cut = [&](int b) -> bool { return b >= 1 && b < kAWarps && s_bj[b] > __ldg(a.crow + r0 + s_bi[b]) - e0; };
+    auto first_cut = [&](int b) -> int {
+        while (b > 1 && s_bi[b - 1] == s_bi[b] && cut(b - 1)) --b;
+        return b;
+    };
+
+    const int is = s_bi[warp], js = s_bj[warp], ie = s_bi[warp + 1], je = s_bj[warp + 1];
+    const bool cut_lo = cut(warp), cut_hi = cut(warp + 1);
+    const T *x_tile0 = static_cast<const T *>(a.x_in) + tile * a.ts_in;
+    const int *colp = a.col + e0;
+    const TV *valp = static_cast<const TV *>(a.val) + e0;
+    const uint32_t ring_w = (uint32_t)__cvta_generic_to_shared(ring) + warp * kTWarpRing;
+    const uint32_t bar_w = (uint32_t)__cvta_generic_to_shared(&s_bar[warp][0]);
+    const uint64_t keep = policy_keep(), stream = policy_stream();
+
+    int rcb = is;
+    auto load_rc = [&](int base) {
+        rcb = base;
+        const int r = base + lane;
+        if (r < nrows) {
+            const int4 *src = reinterpret_cast<const int4 *>(a.rc + r0 + r);
+            int4 *dst = reinterpret_cast<int4 *>(&s_rc[warp][lane]);
+            dst[0] = __ldg(src);
+            dst[1] = __ldg(src + 1);
+        }
+        __syncwarp();
+    };
+    load_rc(is);
+    RowPre pre;
+    auto arm = [&](int i) {
+        if (i < ie) {
+            if (i - rcb >= 32) load_rc(i);
+            pre = issue_row<T, BT>(a, &s_rc[warp][i - rcb], tile, off, stream);
+        }
+    };
+    arm(cut_lo ? is + 1 : is);
+
+    const int n_chunks = (je - js + kTChunk - 1) / kTChunk;
+    int pcol = 0, pcol_nx = js + lane < je ? (int)ld_stream_b32(colp + js + lane, stream) : 0;
+    uint32_t vwin = 0, vwin_nx = js + lane < je ? G::bits(valp + js + lane, stream) : 0u;
+    auto prefetch = [&](int k) {      // chunk k -> stage k % kTStages, whose previous use was read last iteration
+        if (k < n_chunks) {
+            const int cs = js + k * kTChunk, wo = (k * kTChunk) & 31;
+            if (wo == 0) {
+                pcol = pcol_nx;
+                pcol_nx = cs + 32 + lane < je ? (int)ld_stream_b32(colp + cs + 32 + lane, stream) : 0;
+            }
+            const int n_valid = je - cs < kTChunk ? je - cs : kTChunk;
+            const int stage = k % kTStages;
+#if AFB_TMA_ONE_LANE
+            int cc[kTChunk];
+#pragma unroll
+            for (int u = 0; u < kTChunk; ++u) cc[u] = __shfl_sync(kFull, pcol, wo + u);
+#else
+            const int c = __shfl_sync(kFull, pcol, (wo + lane) & 31);
+#endif
+            __syncwarp();
+            if (AFB_TMA_FENCE) fence_proxy_async_smem();
+#if AFB_TMA_ONE_LANE
+            if (lane == 0) {
+                mbar_arrive_expect_tx(bar_w + stage * 8, n_valid * kRowBytes);
+#pragma unroll
+                for (int u = 0; u < kTChunk; ++u)
+                    if (u < n_valid)
+                        bulk_g2s(ring_w + (stage * kTChunk + u) * kRowBytes, x_tile0 + cc[u] * BT, kRowBytes, bar_w + stage * 8, keep);
+            }
+#else
+            if (lane == 0) mbar_arrive_expect_tx(bar_w + stage * 8, n_valid * kRowBytes);
+            if (lane < n_valid)
+                bulk_g2s(ring_w + (stage * kTChunk + lane) * kRowBytes, x_tile0 + c * BT, kRowBytes, bar_w + stage * 8, keep);
+#endif
+        }
+    };
+#pragma unroll
+    for (int st = 0; st < kTStages - 1; ++st) prefetch(st);
+
+    int rend_base = -64, rend = 0;
+    auto row_end = [&](int i) -> int {
+        if (i >= rend_base + 32 || i < rend_base) {
+            rend_base = i;
+            rend = i + lane < nrows ? __ldg(a.crow + r0 + i + lane + 1) - e0 : 0x7fffffff;
+        }
+        return __shfl_sync(kFull, rend, i - rend_base);
+    };
+    int cur = is;
+    int cur_end = cur < nrows ? row_end(cur) : 0x7fffffff;
+    float acc[V];
+#pragma unroll
+    for (int q = 0; q < V; ++q) acc[q] = 0.f;
+    auto close_row = [&](int i) {
+        if (i == is && cut_lo) {
+#pragma unroll
+            for (int q = 0; q < V; ++q) s_first[warp][off + q] = acc[q];
+        } else {
+            finish_row_pre<T, BT>(a, &s_rc[warp][i - rcb], pre, r0 + i, tile, off, acc, stream);
+        }
+#pragma unroll
+        for (int q = 0; q < V; ++q) acc[q] = 0.f;
+        arm(i + 1);
+    };
+
+    bool lost = false;
+    for (int k = 0; k < n_chunks; ++k) {
+        prefetch(k + kTStages - 1);
+        const int stage = k % kTStages;
+        if (!mbar_wait_bounded(bar_w + stage * 8, (k / kTStages) & 1, lost ? kDrainLimit : kWaitLimit, a.err)) {
+            if (!lost && a.err) atomicExch(a.err, 1);
+            lost = true;
+        }
+        const int cs = js + k * kTChunk, wo = (k * kTChunk) & 31;
+        if (wo == 0) {
+            vwin = vwin_nx;
+            vwin_nx = cs + 32 + lane < je ? G::bits(valp + cs + 32 + lane, stream) : 0u;
+        }
+        const uint32_t src = ring_w + stage * (kTChunk * kRowBytes) + lane * 16;
+        if (cs + kTChunk <= cur_end && cs + kTChunk <= je) {
+#pragma unroll
+            for (int u = 0; u < kTChunk; ++u) G::fma(acc, __shfl_sync(kFull, vwin, wo + u), src + u * kRowBytes);
+        } else {
+#pragma unroll
+            for (int u = 0; u < kTChunk; ++u) {
+                const int e = cs + u;
+                if (e < je) {
+                    while (e >= cur_end) {
+                        close_row(cur);
+                        ++cur;
+                        cur_end = row_end(cur);
+                    }
+                    G::fma(acc, __shfl_sync(kFull, vwin, wo + u), src + u * kRowBytes);
+                }
+            }
+        }
+    }
+    while (cur < ie) {
+        close_row(cur);
+        ++cur;
+    }
+    if (lost) {   // let any copy still in flight land before this warp's ring is reused or the CTA exits
+        for (int st = 0; st < kTStages && st < n_chunks; ++st) {
+            const int last = st + ((n_chunks - 1 - st) / kTStages) * kTStages;
+            mbar_wait_bounded(bar_w + st * 8, (last / kTStages) & 1, kDrainLimit, nullptr);
+        }
+    }
+    __syncwarp();
+    float *s_last_w = reinterpret_cast<float *>(ring + warp * kTWarpRing);
+    if (cut_hi) {
+        float *slot = (ie == is && cut_lo) ? s_first[warp] : s_last_w;
+#pragma unroll
+        for (int q = 0; q < V; ++q) slot[off + q] = acc[q];
+    }
+    __syncthreads();
+    const int b = warp + 1;
+    if (b < kAWarps && cut(b) && first_cut(b) == b) {
+        const int row = s_bi[b];
+        const float *s_last_p = reinterpret_cast<const float *>(ring + (b - 1) * kTWarpRing);
+        float sum[V];
+#pragma unroll
+        for (int q = 0; q < V; ++q) sum[q] = s_last_p[off + q];
+        for (int w = b;; ++w) {
+#pragma unroll
+            for (int q = 0; q < V; ++q) sum[q] += s_first[w][off + q];
+            if (!(w + 1 < kAWarps && s_bi[w + 1] == row && cut(w + 1))) break;
+        }
+        finish_row<T, BT>(a, r0 + row, tile, off, sum);
+    }
+}
+
 #ifndef AFB_ASYNC
 #define AFB_ASYNC 1
 #endif
 
 template <typename T, typename TV>
 void launch(const StepArgs &a, cudaStream_t s) {
-    constexpr int BT = (AFB_ASYNC ? 32 : kLanesPerEdge) * Lane<T>::V;
+    constexpr int BT = (AFB_ASYNC || AFB_TMA ? 32 : kLanesPerEdge) * Lane<T>::V;
     if (a.n_items == 0 || a.batch == 0) return;
     const int64_t tiles = (a.batch + BT - 1) / BT;
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
-    if (AFB_ASYNC) {
+    if (AFB_TMA) {
+        static unsigned long long configured = 0;   // devices on which this instantiation may use kTRingBytes
+        int dev = 0;
+        AFB_CUDA(cudaGetDevice(&dev));
+        if (dev < 64 && !(configured >> dev & 1ull)) {
+            AFB_CUDA(cudaFuncSetAttribute(step_kernel_tma<T, TV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTRingBytes));
+            configured |= 1ull << dev;
+        }
+        step_kernel_tma<T, TV><<<(unsigned)blocks, kAWarps * 32, kTRingBytes, s>>>(a);
+    } else if (AFB_ASYNC) {
         static unsigned long long configured = 0;   // devices on which this instantiation may use kRingBytes
         int dev = 0;
         AFB_CUDA(cudaGetDevice(&dev));
@@ -660,11 +974,11 @@ __global__ void bounds_kernel(int n_items, int warps, const int *__restrict__ cr
     }
 }
 
-int tile_cols(int elem_bytes) { return (AFB_ASYNC ? 32 : kLanesPerEdge) * (16 / elem_bytes); }
+int tile_cols(int elem_bytes) { return (AFB_ASYNC || AFB_TMA ? 32 : kLanesPerEdge) * (16 / elem_bytes); }
 void launch_step_dev16(const StepArgs &a, cudaStream_t s) { launch<__half, __half>(a, s); }
 
 void build_bounds(Csr &m, cudaStream_t s) {
-    const int warps = AFB_ASYNC ? kAWarps : kWarps;
+    const int warps = AFB_ASYNC || AFB_TMA ? kAWarps : kWarps;
     m.bounds.alloc((size_t)m.n_items * (warps + 1));
     if (m.n_items) {
         bounds_kernel<<<grid_for((int64_t)m.n_items * (warps + 1), 256), 256, 0, s>>>(m.n_items, warps, m.crow.get(),

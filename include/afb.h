@@ -125,6 +125,11 @@ AFB_API int afb_cone_forward_timed(const afb_cone *cone, int mode, const void *u
                            float *out, int64_t ld_out, void *workspace, size_t workspace_bytes,
                            void *const *events, void *stream);
 
+/* Device status of the handle's kernels, copied to *status (HOST): 0 = ok, 1 = a bounded wait of a
+ * step kernel gave up (a gather never completed; that forward's output is not valid).  With reset != 0
+ * the word is cleared.  Synchronous on `stream`. */
+AFB_API int afb_cone_status(const afb_cone *cone, int *status, int reset, void *stream);
+
 /* ---- the literal recurrence over all neurons --------------------------------------------------
  * Replaces ConnectomeRNN.forward's no-grad branch (chessfly/brain.py:211-223): from h = 0,
  * `steps` times  h <- lerp(h, clamp(W h + b + u, 0, h_max), alpha)  over all n neurons, float32.
@@ -134,6 +139,7 @@ typedef struct afb_graph afb_graph;
 AFB_API int afb_graph_create(afb_graph **graph, int64_t n, int64_t e, const int64_t *pre, const int64_t *post,
                      void *stream);
 AFB_API void afb_graph_destroy(afb_graph *graph);
+AFB_API int afb_graph_status(const afb_graph *graph, int *status, int reset, void *stream);
 AFB_API size_t afb_graph_forward_workspace(const afb_graph *graph, int64_t batch);
 AFB_API int afb_graph_forward(const afb_graph *graph, const float *w, const float *bias, const float *alpha_logit,
                       float h_max, const float *u, int64_t ld_u, int64_t batch, int steps, float *h,

@@ -111,6 +111,7 @@ def test_small_forward_io_float32_matches_reference(small):
     err = orc.rel_l2(out, g["fwd_io_f64"])
     assert err < F32_GATE, err
     assert orc.rel_l2(out, g["fwd_io_f32"]) < F32_GATE
+    assert rnn.device_status() == 0
 
 
 def test_small_literal_forward_matches_reference(small):
@@ -244,3 +245,4 @@ def test_columns_are_independent_at_full_batch(full):
     assert wide.shape == (len(inst.out_idx), 35840)
     for k in (0, 33, 69):
         torch.testing.assert_close(wide[:, k * 512:(k + 1) * 512], narrow, rtol=0, atol=0)
+    assert rnn.device_status() == 0
