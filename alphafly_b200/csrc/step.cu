@@ -202,9 +202,9 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
             }
         }
 #pragma unroll
-        for (int off = kLanesPerEdge; off < 32; off <<= 1)
+        for (int sh = kLanesPerEdge; sh < 32; sh <<= 1)
 #pragma unroll
-            for (int q = 0; q < V; ++q) acc[q] += __shfl_xor_sync(kFull, acc[q], off);
+            for (int q = 0; q < V; ++q) acc[q] += __shfl_xor_sync(kFull, acc[q], sh);
         const bool span_lo = (i == is) && cut_lo, span_hi = (i == ie) && cut_hi;
         if (span_lo || span_hi) {
             // a cut row: its first partial goes to s_first of every warp that starts inside it, the
@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(kAWarps * 32, AFB_ASYNC_MINBLOCKS) step_kernel
     using G = Gather<T>;
     constexpr int V = G::V;
     constexpr int BT = 32 * V;
-    extern __shared__ __align__(16) unsigned char ring[];
+    extern __shared__ __align__(128) unsigned char ring[];
     __shared__ float s_first[kAWarps][BT];
     __shared__ __align__(16) RowConst s_rc[kAWarps][32];
     __shared__ int s_bi[kAWarps + 1], s_bj[kAWarps + 1];
