@@ -5,6 +5,8 @@
 // trajectory c_t by T full batch-1 SpMVs; per step the row constants of the chosen mode (for float32,
 // k_t = (W c_{t-1} + b)[R_t] - A_t c_{t-1}[R_{t-1}] with one warp per row); the sub-matrix values
 // w[edges].  afb_cone_forward then runs one fused step kernel per step and one output kernel.
+#include <mutex>
+
 #include "internal.cuh"
 
 namespace afb {
@@ -323,6 +325,54 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
         }
         launch_output((int)n, nullptr, nullptr, 0, x_in, 0, ts, h, ld_h, batch, s);   // row-for-row copy
     });
+}
+
+// ---- forward without any allocation -----------------------------------------------------------
+// Some callers cannot allocate device memory when they evaluate: a host process whose device memory
+// is owned by another framework's pooling allocator (a cudaMalloc behind its back fragments the pool
+// or fails against its reservation), or a latency-bound serving loop that cannot afford the implicit
+// device synchronisation of cudaMalloc / cudaFree.  For them the forward's two ping-pong state
+// buffers live in this file-scope device array instead of a caller workspace.  Its size is fixed:
+// every GPU that loads the library holds these 32 MiB until the process exits.
+#define AFB_NOALLOC_SCRATCH_BYTES (32u << 20)
+static __device__ __align__(256) unsigned char g_noalloc_scratch[AFB_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+// Device address of g_noalloc_scratch on the current device.  In host code the symbol's name is a
+// host-side stand-in, not a device address, so it is resolved once per device with cudaGetSymbolAddress
+// (with that device current) and cached.
+void *noalloc_scratch() {
+    static std::mutex lock;
+    static void *addr[64] = {};
+    int dev = 0;
+    AFB_CUDA(cudaGetDevice(&dev));
+    AFB_CHECK(dev >= 0 && dev < 64, "device index out of range for the built-in scratch");
+    std::lock_guard<std::mutex> g(lock);
+    if (!addr[dev]) {
+        void *p = nullptr;
+        AFB_CUDA(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+        addr[dev] = p;
+    }
+    return addr[dev];
+}
+}  // namespace
+
+int afb_cone_forward_noalloc(const afb_cone *c, int mode, const void *u_in, int64_t ld_u, int64_t batch, float *out,
+                             int64_t ld_out, void *stream) {
+    void *ws = nullptr;
+    const int rc = guarded([&] {
+        AFB_CHECK(c, "cone is NULL");
+        AFB_CHECK(mode == AFB_MODE_F32 || mode == AFB_MODE_DEV16, "unknown mode");
+        AFB_CHECK(batch >= 0, "batch must be >= 0");
+        const size_t need = afb_cone_forward_workspace(c, mode, batch);
+        AFB_CHECK(need <= AFB_NOALLOC_SCRATCH_BYTES,
+                  "afb_cone_forward_noalloc: this cone and batch need " + std::to_string(need) +
+                      " bytes of state, more than the built-in scratch of " + std::to_string(AFB_NOALLOC_SCRATCH_BYTES) +
+                      " bytes; use afb_cone_forward with a caller-provided workspace or a smaller batch");
+        ws = noalloc_scratch();
+    });
+    if (rc != AFB_OK) return rc;
+    return afb_cone_forward_timed(c, mode, u_in, ld_u, batch, out, ld_out, ws, AFB_NOALLOC_SCRATCH_BYTES, nullptr, stream);
 }
 
 }  // extern "C"

@@ -125,6 +125,19 @@ AFB_API int afb_cone_forward_timed(const afb_cone *cone, int mode, const void *u
                            float *out, int64_t ld_out, void *workspace, size_t workspace_bytes,
                            void *const *events, void *stream);
 
+/* As afb_cone_forward, but allocating nothing and taking no workspace: for callers that cannot
+ * allocate device memory at evaluation time (their device memory belongs to another framework's pool,
+ * or their serving loop cannot take cudaMalloc's implicit synchronisation).  No counterpart in the
+ * reference, which always allocates through torch.  The state lives in a fixed 32 MiB device array
+ * built into the library (held on every GPU that loads it until the process exits); a cone and batch
+ * whose afb_cone_forward_workspace() exceeds 32 MiB are rejected with AFB_EINVAL.  The first call on a
+ * device resolves that array's device address (cudaGetSymbolAddress) and should come before any stream
+ * capture on that device.  The array needs no clearing (every step overwrites what the next reads).
+ * All calls on a device share it: calls whose work overlaps on the GPU (other streams, other cones)
+ * race and corrupt each other's results; order them. */
+AFB_API int afb_cone_forward_noalloc(const afb_cone *cone, int mode, const void *u_in, int64_t ld_u, int64_t batch,
+                                     float *out, int64_t ld_out, void *stream);
+
 /* Device status of the handle's kernels, copied to *status (HOST): 0 = ok, 1 = a bounded wait of a
  * step kernel gave up (a gather never completed; that forward's output is not valid).  With reset != 0
  * the word is cleared.  Synchronous on `stream`. */
