@@ -43,6 +43,10 @@ SIGNATURES = {
     "afb_cone_forward_timed": (_int, [_p, _int, _p, _i64, _i64, _p, _i64, _p, _sz, _p, _p]),
     "afb_cone_forward_noalloc": (_int, [_p, _int, _p, _i64, _i64, _p, _i64, _p]),
     "afb_cone_status": (_int, [_p, _p, _int, _p]),
+    "afb_cone_train_workspace": (_sz, [_p, _i64]),
+    "afb_cone_forward_train": (_int, [_p, _p, _i64, _i64, _p, _i64, _p, _sz, _p]),
+    "afb_cone_backward_workspace": (_sz, [_p, _i64]),
+    "afb_cone_backward": (_int, [_p, _p, _i64, _i64, _p, _sz, _p, _i64, _p, _p, _p, _p, _sz, _p]),
     "afb_graph_status": (_int, [_p, _p, _int, _p]),
     "afb_graph_create": (_int, [_pp, _i64, _i64, _p, _p, _p]),
     "afb_graph_destroy": (None, [_p]),

@@ -10,7 +10,9 @@ search / training callers use it unchanged.  The work runs in the CUDA library:
 * ``light_cone``  builds the per-step row sets, sub-matrices and maps on the GPU (``afb_cone_create``);
 * ``forward_io``  (no grad) runs the fused SpMM step kernel once per step, float32 state for float32
   input, float16 deviation from the resting trajectory for float16 input (``afb_cone_forward``);
-* ``forward``     (no grad) runs the literal recurrence over all neurons (``afb_graph_forward``).
+  with autograd it runs the float32 training forward and the library's backward (``_ConeTrain``);
+* ``forward``     (no grad) runs the literal recurrence over all neurons (``afb_graph_forward``); with
+  autograd, the same training path over the cone whose inputs and outputs are all neurons.
 
 There is no CPU path: on CPU tensors these methods raise ``RuntimeError``.
 """
@@ -169,14 +171,20 @@ class LightCone:
         """(Re)compute the weight-dependent constants of ``mode`` unless ``key`` is unchanged."""
         if self._weights.get(mode) == key:
             return
-        with torch.no_grad(), torch.cuda.device(self.device):
-            w = rnn.edge_weights().float().contiguous()
-            bias = rnn.bias.detach().float().contiguous()
-            alpha_logit = rnn.alpha_logit.detach().float().contiguous()
-            h_max = float("inf") if rnn.h_max is None else float(rnn.h_max)
-            _lib.check(self._lib.afb_cone_set_weights(self._h, mode, _ptr(w), _ptr(bias), _ptr(alpha_logit), h_max,
-                                                      _stream(self.device)))
+        with torch.no_grad():
+            self.set_weight_tensors(mode, rnn.edge_weights(), rnn.bias, rnn.alpha_logit, rnn.h_max)
         self._weights[mode] = key
+
+    def set_weight_tensors(self, mode: int, w, bias, alpha_logit, h_max) -> None:
+        """Constants of ``mode`` from explicit edge weights, bias and alpha logits (``afb_cone_set_weights``)."""
+        self._weights.pop(mode, None)
+        with torch.cuda.device(self.device):
+            w = w.detach().float().contiguous()
+            bias = bias.detach().float().contiguous()
+            alpha_logit = alpha_logit.detach().float().contiguous()
+            h = float("inf") if h_max is None else float(h_max)
+            _lib.check(self._lib.afb_cone_set_weights(self._h, mode, _ptr(w), _ptr(bias), _ptr(alpha_logit), h,
+                                                      _stream(self.device)))
 
     def status(self, reset: bool = True) -> int:
         """Device status word of this cone's step kernels: 0 = ok, 1 = a bounded wait gave up (some
@@ -266,6 +274,56 @@ class _EdgeWeights(torch.autograd.Function):
         return grad_w * w.to(grad_w.dtype), None, None
 
 
+class _ConeTrain(torch.autograd.Function):
+    """forward_io with autograd (chessfly/brain.py:289-294, 315-329): the library's float32 training
+    forward keeps every step's state, and its backward returns dL/du_in, dL/dw, dL/db and dL/dalpha in
+    one pass (``afb_cone_backward``).  Inputs: u_in (I, B) float32, w (E) = edge weights (autograd links
+    them to log_gain), bias (N), alpha_logit (N)."""
+
+    @staticmethod
+    def forward(ctx, u_in, w, bias, alpha_logit, cone, h_max):
+        dev = cone.device
+        batch = u_in.shape[1]
+        u_in = u_in.contiguous()
+        cone.set_weight_tensors(_lib.MODE_F32, w, bias, alpha_logit, h_max)
+        lib = cone._lib
+        with torch.cuda.device(dev):
+            saved_bytes = lib.afb_cone_train_workspace(cone._h, batch)
+            saved = torch.empty(saved_bytes, dtype=torch.uint8, device=dev)
+            out = torch.empty(cone.n_out, batch, dtype=torch.float32, device=dev)
+            _lib.check(lib.afb_cone_forward_train(cone._h, _ptr(u_in), u_in.stride(0), batch, _ptr(out), batch,
+                                                  _ptr(saved), saved_bytes, _stream(dev)))
+        ctx.cone, ctx.h_max, ctx.batch, ctx.n_in, ctx.saved_state = cone, h_max, batch, u_in.shape[0], saved
+        ctx.save_for_backward(w.detach(), bias.detach(), alpha_logit.detach())
+        return out
+
+    @staticmethod
+    def backward(ctx, g_out):
+        cone, batch = ctx.cone, ctx.batch
+        w, bias, alpha_logit = ctx.saved_tensors
+        dev = cone.device
+        lib = cone._lib
+        # the cone's constants must be those of this forward's weights
+        cone.set_weight_tensors(_lib.MODE_F32, w, bias, alpha_logit, ctx.h_max)
+        g_out = g_out.float().contiguous()
+        with torch.cuda.device(dev):
+            ws_bytes = lib.afb_cone_backward_workspace(cone._h, batch)
+            ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+            g_u = torch.empty(ctx.n_in, batch, dtype=torch.float32, device=dev)
+            g_w = torch.empty_like(w, dtype=torch.float32)
+            g_b = torch.empty_like(bias, dtype=torch.float32)
+            g_a = torch.empty_like(alpha_logit, dtype=torch.float32)
+            saved = ctx.saved_state
+            _lib.check(lib.afb_cone_backward(cone._h, _ptr(g_out), g_out.stride(0), batch, _ptr(saved), saved.numel(),
+                                             _ptr(g_u), batch, _ptr(g_w), _ptr(g_b), _ptr(g_a), _ptr(ws), ws_bytes,
+                                             _stream(dev)))
+        ctx.saved_state = None
+        alpha = torch.sigmoid(alpha_logit.float())
+        g_logit = g_a * alpha * (1 - alpha)
+        return (g_u if ctx.needs_input_grad[0] else None, g_w.to(w.dtype), g_b.to(bias.dtype),
+                g_logit.to(alpha_logit.dtype), None, None)
+
+
 class ConnectomeRNN(nn.Module):
     def __init__(self, conn: Connectome, alpha_init: float = 0.5, bias_init: float = 0.0,
                  global_scale: float = 1.0, h_max: float | None = 10.0):
@@ -314,12 +372,21 @@ class ConnectomeRNN(nn.Module):
         (chessfly/brain.py:218), ``u`` is not modified."""
         assert u.is_contiguous()
         _require_cuda(u, "u")
-        if torch.is_grad_enabled() and (u.requires_grad or any(p.requires_grad for p in self.parameters())):
-            raise NotImplementedError("alphafly_b200: the training path of forward() is not available yet")
         if u.dtype not in (torch.float32, torch.float16):
             raise TypeError(f"alphafly_b200 computes in float32 or float16, got {u.dtype}")
+        if torch.is_grad_enabled() and (u.requires_grad or any(p.requires_grad for p in self.parameters())):
+            # the literal recurrence is the light cone with every neuron an input and an output
+            everyone = self._everyone()
+            cone = self.light_cone(everyone, everyone, steps)
+            h = _ConeTrain.apply(u.float(), self.edge_weights(), self.bias, self.alpha_logit, cone, self.h_max)
+            return h.to(u.dtype)
         h = self._graph().forward(self, u.float().contiguous(), steps)
         return h.to(u.dtype)
+
+    def _everyone(self) -> torch.Tensor:
+        if getattr(self, "_all_idx", None) is None or self._all_idx.device != self.pre.device:
+            self._all_idx = torch.arange(self.n, device=self.pre.device)
+        return self._all_idx
 
     def device_status(self, reset: bool = True) -> int:
         """0 if every native kernel since the last reset completed normally, else the library's status
@@ -350,7 +417,8 @@ class ConnectomeRNN(nn.Module):
             raise TypeError(f"alphafly_b200 computes in float32 or float16, got {u_in.dtype}")
         cone = self.light_cone(in_idx, out_idx, steps)
         if torch.is_grad_enabled():
-            raise NotImplementedError("alphafly_b200: the training path of forward_io() is not available yet")
+            out = _ConeTrain.apply(u_in.float(), self.edge_weights(), self.bias, self.alpha_logit, cone, self.h_max)
+            return out.to(u_in.dtype)
         mode = _lib.MODE_DEV16 if u_in.dtype == torch.float16 else _lib.MODE_F32
         cone.set_weights(self, mode, self._weight_key(mode, cone))
         u_in = u_in if u_in.stride(1) == 1 else u_in.contiguous()

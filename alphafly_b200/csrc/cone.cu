@@ -103,6 +103,20 @@ __global__ void local_edges(const int *__restrict__ edges, const int *__restrict
     }
 }
 
+__global__ void full_keys(const int *__restrict__ post, const int *__restrict__ pre, long long *__restrict__ key,
+                          int *__restrict__ iota, int64_t n, int64_t e) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < e; i += (int64_t)gridDim.x * blockDim.x) {
+        key[i] = (long long)pre[i] * n + post[i];
+        iota[i] = (int)i;
+    }
+}
+
+// inv[prev[i]] = i for the carried rows i of R_t (prev is one-to-one onto its image)
+__global__ void invert_prev(const int *__restrict__ prev, int n_rows, int *__restrict__ inv) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_rows; i += gridDim.x * blockDim.x)
+        if (prev[i] >= 0) inv[prev[i]] = i;
+}
+
 __global__ void widen(const int *__restrict__ src, int64_t *__restrict__ dst, int64_t m, int mode) {
     // mode 0: copy; mode 1: (v >= 0) as 0/1; mode 2: max(v, 0)
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x) {
@@ -232,7 +246,27 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
             AFB_CHECK(to_host(bad.get(), 1, s)[0] == 0, "edges must be sorted by (post, pre), the CSR order of W[post, pre]");
         }
         crow_from_rows(post32.get(), e, (int)n, c->full_crow, tmp, s);
+        // W^T: edges sorted by (pre, post), stable (the reference's t_order, brain.py:192-195)
+        c->full_torder.alloc(e ? e : 1);
+        c->full_tcol.alloc(e ? e : 1);
+        if (e) {
+            DevBuf<long long> key(e), key_sorted(e);
+            DevBuf<int> iota(e);
+            full_keys<<<grid_for(e, kBlock), kBlock, 0, s>>>(post32.get(), pre32.get(), key.get(), iota.get(), n, e);
+            AFB_LAUNCHED();
+            size_t bytes = 0;
+            const int end_bit = bits_for((long long)n * n);
+            AFB_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, bytes, key.get(), key_sorted.get(), iota.get(),
+                                                     c->full_torder.get(), (int)e, 0, end_bit, s));
+            AFB_CUDA(cub::DeviceRadixSort::SortPairs(tmp.need(bytes), bytes, key.get(), key_sorted.get(), iota.get(),
+                                                     c->full_torder.get(), (int)e, 0, end_bit, s));
+            gather_int<<<grid_for(e, kBlock), kBlock, 0, s>>>(post32.get(), c->full_torder.get(), c->full_tcol.get(), (int)e);
+            AFB_LAUNCHED();
+        }
+        crow_from_rows(pre32.get(), e, (int)n, c->full_tcrow, tmp, s);
         c->full_col = std::move(pre32);
+        c->full_post = std::move(post32);
+        const int *post32_p = c->full_post.get();
 
         // V_t (forward reachability from the inputs) and D_t (backward reachability of the outputs)
         const int T = steps;
@@ -242,12 +276,12 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
         if (n_in) fill_mask<<<grid_for(n_in, kBlock), kBlock, 0, s>>>(V.get() + n, in32.get(), n_in);
         for (int t = 2; t <= T; ++t) {
             AFB_CUDA(cudaMemcpyAsync(V.get() + t * n, V.get() + (t - 1) * n, n, cudaMemcpyDeviceToDevice, s));
-            if (e) hop<<<grid_for(e, kBlock), kBlock, 0, s>>>(V.get() + (t - 1) * n, V.get() + t * n, c->full_col.get(), post32.get(), e);
+            if (e) hop<<<grid_for(e, kBlock), kBlock, 0, s>>>(V.get() + (t - 1) * n, V.get() + t * n, c->full_col.get(), post32_p, e);
         }
         fill_mask<<<grid_for(n_out, kBlock), kBlock, 0, s>>>(D.get() + (size_t)T * n, c->out_idx.get(), n_out);
         for (int t = T - 1; t >= 0; --t) {
             AFB_CUDA(cudaMemcpyAsync(D.get() + t * n, D.get() + (t + 1) * n, n, cudaMemcpyDeviceToDevice, s));
-            if (e) hop<<<grid_for(e, kBlock), kBlock, 0, s>>>(D.get() + (t + 1) * n, D.get() + t * n, post32.get(), c->full_col.get(), e);
+            if (e) hop<<<grid_for(e, kBlock), kBlock, 0, s>>>(D.get() + (t + 1) * n, D.get() + t * n, post32_p, c->full_col.get(), e);
         }
         AFB_LAUNCHED();
         c->st.resize(T + 1);
@@ -277,6 +311,9 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
                 gather_int<<<grid_for(nr, kBlock), kBlock, 0, s>>>(in_pos.get(), sp.rows.get(), sp.usrc.get(), nr);
             }
             AFB_LAUNCHED();
+            sp.inv_prev.alloc(nc ? nc : 1);
+            if (nc) fill_int<<<grid_for(nc, kBlock), kBlock, 0, s>>>(sp.inv_prev.get(), -1, nc);
+            if (nr) invert_prev<<<grid_for(nr, kBlock), kBlock, 0, s>>>(sp.prev.get(), nr, sp.inv_prev.get());
             // carried rows (brain.py:161-165) and fed rows (brain.py:166-168)
             if (nr) nonneg_flags<<<grid_for(nr, kBlock), kBlock, 0, s>>>(sp.prev.get(), rflags.get(), nr);
             sp.n_keep = select_flagged(rflags.get(), nr, sp.keep_next, tmp, s);
@@ -294,7 +331,7 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
             m.n_cols = nc;
             m.present = nc > 0;
             if (m.present && e) {
-                edge_flags<<<grid_for(e, kBlock), kBlock, 0, s>>>(post32.get(), c->full_col.get(), where_next.get(), where_prev.get(), eflags.get(), e);
+                edge_flags<<<grid_for(e, kBlock), kBlock, 0, s>>>(post32_p, c->full_col.get(), where_next.get(), where_prev.get(), eflags.get(), e);
                 AFB_LAUNCHED();
                 m.nnz = select_flagged(eflags.get(), e, m.edges, tmp, s);
             } else {
@@ -309,7 +346,7 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
             if (nnz) {
                 DevBuf<long long> key(nnz), key_sorted(nnz);
                 DevBuf<int> iota(nnz);
-                local_edges<<<grid_for(nnz, kBlock), kBlock, 0, s>>>(m.edges.get(), post32.get(), c->full_col.get(), where_next.get(),
+                local_edges<<<grid_for(nnz, kBlock), kBlock, 0, s>>>(m.edges.get(), post32_p, c->full_col.get(), where_next.get(),
                                                                      where_prev.get(), m.post.get(), m.col.get(), key.get(), iota.get(), nr, nnz);
                 AFB_LAUNCHED();
                 // stable radix sort: equal keys (duplicate synapses) keep edge order

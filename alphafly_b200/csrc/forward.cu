@@ -107,6 +107,16 @@ __global__ void graph_constants(int64_t n, const float *__restrict__ bias, const
     }
 }
 
+__global__ void gather_float(const float *__restrict__ table, const int *__restrict__ ids, float *__restrict__ out, int64_t m);
+}  // namespace
+
+void gather_floats(const float *table, const int *ids, float *out, int64_t m, cudaStream_t s) {
+    if (m <= 0) return;
+    gather_float<<<grid_for(m, kBlock), kBlock, 0, s>>>(table, ids, out, m);
+    AFB_LAUNCHED();
+}
+
+namespace {
 __global__ void gather_float(const float *__restrict__ table, const int *__restrict__ ids, float *__restrict__ out, int64_t m) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < m; i += (int64_t)gridDim.x * blockDim.x)
         out[i] = table[ids[i]];
@@ -148,6 +158,7 @@ int afb_cone_set_weights(afb_cone *c, int mode, const float *w, const float *bia
         }
         if (!c->out_base[mode].p) c->out_base[mode].alloc(c->n_out);
         c->ready[mode] = false;
+        c->h_max = h_max;
         sigmoid_kernel<<<grid_for(n, kBlock), kBlock, 0, s>>>(n, alpha_logit, c->alpha.get());
         AFB_CUDA(cudaMemsetAsync(c->resting.get(), 0, n * sizeof(float), s));
         float *wc = c->wc.get();
@@ -173,6 +184,10 @@ int afb_cone_set_weights(afb_cone *c, int mode, const float *w, const float *bia
                                                                         mode == AFB_MODE_DEV16 ? sp.val16.get() : nullptr);
                 AFB_LAUNCHED();
             }
+            if (mode == AFB_MODE_F32 && m.nnz) {   // values of the transpose, for the training backward
+                if (sp.val32_t.n < (size_t)m.nnz) sp.val32_t.alloc(m.nnz);
+                gather_floats(sp.val32.get(), m.t_order.get(), sp.val32_t.get(), m.nnz, s);
+            }
             if (sp.rc[mode].n < (size_t)sp.n_rows) sp.rc[mode].alloc(sp.n_rows);
             if (sp.n_rows) {
                 row_constants<<<grid_for((int64_t)sp.n_rows * 32, kBlock, 148 * 64), kBlock, 0, s>>>(
@@ -181,6 +196,10 @@ int afb_cone_set_weights(afb_cone *c, int mode, const float *w, const float *bia
                     c->resting.get() + (size_t)(t - 1) * n, c->alpha.get(), h_max, sp.rc[mode].get());
                 AFB_LAUNCHED();
             }
+        }
+        if (mode == AFB_MODE_F32 && c->e) {
+            if (!c->w_t.p) c->w_t.alloc(c->e);
+            gather_floats(w, c->full_torder.get(), c->w_t.get(), c->e, s);
         }
         gather_float<<<grid_for(c->n_out, kBlock), kBlock, 0, s>>>(c->resting.get() + (size_t)T * n, c->out_idx.get(),
                                                                  c->out_base[mode].get(), c->n_out);

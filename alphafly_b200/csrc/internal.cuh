@@ -42,7 +42,9 @@ struct Step {
     DevBuf<int> keep_next, keep_prev, u_pos, u_src;
     int n_keep = 0, n_fed = 0;
     DevBuf<RowConst> rc[2];        // per mode
+    DevBuf<int> inv_prev;          // (|R_{t-1}|) the row of R_t carried from each row of R_{t-1}, or -1
     DevBuf<float> val32;           // w[edges], AFB_MODE_F32
+    DevBuf<float> val32_t;         // w[edges[t_order]], the transpose's values (training)
     DevBuf<__half> val16;          // half(w[edges]), AFB_MODE_DEV16
 };
 
@@ -81,6 +83,7 @@ struct StepArgs {
     int64_t ts_out;
     int64_t batch;
     int *err;                      // device status word: set non-zero when a bounded wait gives up
+    float *y_out;                  // training forward: pre-clamp drive of R_t, tile-major (float32 state only)
 };
 
 // Batch columns one CTA covers for a state element of `elem_bytes`; the state's leading dimension is
@@ -100,6 +103,9 @@ void launch_step_dev16(const StepArgs &a, cudaStream_t s);
 void launch_output(int n_out, const int *src, const float *base, int add_base, const void *state, int state_is_half,
                    int64_t ts_state, float *out, int64_t ld_out, int64_t batch, cudaStream_t s);
 
+// out[i] = table[ids[i]], i < m
+void gather_floats(const float *table, const int *ids, float *out, int64_t m, cudaStream_t s);
+
 // Warp-per-row y = A x for one column vector (float32), A given by (crow, col, val).
 void launch_spmv(int n_rows, const int *crow, const int *col, const float *val, const float *x, float *y,
                  cudaStream_t s);
@@ -110,7 +116,8 @@ struct afb_cone {
     int64_t n = 0, e = 0;
     int steps = 0;
     std::vector<afb::Step> st;        // st[0..steps]; st[0] holds R_0 only
-    afb::DevBuf<int> full_crow, full_col;
+    afb::DevBuf<int> full_crow, full_col, full_post;   // W in CSR (edge order) with each edge's row
+    afb::DevBuf<int> full_tcrow, full_tcol, full_torder; // W^T in CSR and the edge permutation into it
     int64_t n_in = 0, n_out = 0;
     afb::DevBuf<int> out_idx, out_row, out_pos, out_src;
     int n_hit = 0;
@@ -121,9 +128,11 @@ struct afb_cone {
     afb::DevBuf<float> resting;        // (steps + 1) x n
     afb::DevBuf<float> kfull;          // (steps + 1) x n: W c_{t-1} + b
     afb::DevBuf<float> wc;             // (n) scratch of the resting-trajectory SpMV
+    afb::DevBuf<float> w_t;            // (e) w[full_torder]: values of W^T (training)
     afb::DevBuf<float> out_base[2];    // c_T[out_idx], per mode
     bool ready[2] = {false, false};    // per mode: constants set since the handle was built
     afb::DevBuf<int> err;              // device status word of the step kernels (0 = ok)
+    float h_max = 10.f;                // clamp of the last afb_cone_set_weights
 };
 
 struct afb_graph {

@@ -123,6 +123,8 @@ __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t t
         o[k] = p[k] + al * (x - p[k]);
     }
     Lane<T>::store(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off, o);
+    if constexpr (sizeof(T) == 4)
+        if (a.y_out) Lane<float>::store(a.y_out + tile * a.ts_out + (int64_t)row * BT + off, y);
 }
 
 template <typename T, typename TV>
@@ -479,15 +481,17 @@ __device__ __forceinline__ void finish_row_pre(const StepArgs &a, const RowConst
             for (int k = 0; k < V; ++k) ux[k] = col0 + k < a.batch ? Lane<T>::scalar(u + k) : 0.f;
         }
     }
-    float o[V];
+    float o[V], yv[V];
 #pragma unroll
     for (int k = 0; k < V; ++k) {
-        const float y = acc[k] + kk + (usrc >= 0 ? ux[k] : 0.f);
-        const float x = fminf(fmaxf(y, lo), hi) + e;
+        yv[k] = acc[k] + kk + (usrc >= 0 ? ux[k] : 0.f);
+        const float x = fminf(fmaxf(yv[k], lo), hi) + e;
         const float pk = prev >= 0 ? p[k] : pc;
         o[k] = pk + al * (x - pk);
     }
     store_stream<T>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off, o, stream);
+    if constexpr (sizeof(T) == 4)
+        if (a.y_out) Lane<float>::store(a.y_out + tile * a.ts_out + (int64_t)row * BT + off, yv);
 }
 
 template <typename T, typename TV>

@@ -143,6 +143,25 @@ AFB_API int afb_cone_forward_noalloc(const afb_cone *cone, int mode, const void 
  * the word is cleared.  Synchronous on `stream`. */
 AFB_API int afb_cone_status(const afb_cone *cone, int *status, int reset, void *stream);
 
+/* ---- training: forward with saved state, and backward -----------------------------------------
+ * Replaces forward_io with autograd enabled (chessfly/brain.py:289-294, 315-329) and the backward of
+ * _SparseRecurrent (brain.py:78-99) and _constants (brain.py:238-252).  float32 only; needs
+ * afb_cone_set_weights(AFB_MODE_F32) with the current weights.
+ * afb_cone_forward_train: as afb_cone_forward(AFB_MODE_F32), keeping every step's state and pre-clamp
+ *   drive in `saved` (afb_cone_train_workspace bytes, 256-byte aligned) for afb_cone_backward.
+ * afb_cone_backward: given dL/dout (n_out, batch), writes dL/du_in (n_in, batch), dL/dw (E), dL/db (n)
+ *   and dL/dalpha (n, alpha = sigmoid(alpha_logit)); the chain rule to log_gain (dL/dw * w) and to
+ *   alpha_logit (dL/dalpha * alpha (1 - alpha)) is the caller's.  workspace: afb_cone_backward_workspace
+ *   bytes, 256-byte aligned, no initialisation needed.  Deterministic: no floating-point atomics except
+ *   where two output positions name the same neuron. */
+AFB_API size_t afb_cone_train_workspace(const afb_cone *cone, int64_t batch);
+AFB_API int afb_cone_forward_train(const afb_cone *cone, const float *u_in, int64_t ld_u, int64_t batch, float *out,
+                                   int64_t ld_out, void *saved, size_t saved_bytes, void *stream);
+AFB_API size_t afb_cone_backward_workspace(const afb_cone *cone, int64_t batch);
+AFB_API int afb_cone_backward(const afb_cone *cone, const float *g_out, int64_t ld_g, int64_t batch, const void *saved,
+                              size_t saved_bytes, float *g_u_in, int64_t ld_gu, float *g_w, float *g_bias, float *g_alpha,
+                              void *workspace, size_t workspace_bytes, void *stream);
+
 /* ---- the literal recurrence over all neurons --------------------------------------------------
  * Replaces ConnectomeRNN.forward's no-grad branch (chessfly/brain.py:211-223): from h = 0,
  * `steps` times  h <- lerp(h, clamp(W h + b + u, 0, h_max), alpha)  over all n neurons, float32.
