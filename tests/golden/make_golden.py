@@ -14,6 +14,11 @@ with ``alphafly_b200.synth``, writes the instance's w0 and parameters into the r
   * shuffled.npz  configuration 4: LightCone hashes, forward_io float32 at B=16
   * full.npz      configuration 2 graph: LightCone sizes and hashes (6 steps), forward_io float32 at
                   B=8, forward (no pruning) float32 at B=4
+  * model.npz     FlyChessNet on the 60-neuron test graph (tests/test_core.py:404): the initial
+                  state_dict, eval-mode float32 logits, and one train_step (chessfly/train.py:126-138) with
+                  its losses, clipped gradients, updated parameters and RunningNorm statistics
+The reference's trainer imports modules that use python-chess at import time; a permissive stand-in
+module (every attribute a neutral dummy) is installed for them.  It is never called on the network path.
 Index arrays too large to store are pinned by the SHA-256 of their int64 little-endian bytes.
 """
 
@@ -201,17 +206,119 @@ def make_full(brain) -> dict:
     return rec
 
 
+class _Dummy:
+    """A neutral stand-in value for python-chess attributes used at import time by the reference's
+    search modules; the network and trainer never call them."""
+
+    def __getattr__(self, k):
+        return _Dummy()
+
+    def __call__(self, *a, **k):
+        return _Dummy()
+
+    def __iter__(self):
+        return iter(())
+
+    def __int__(self):
+        return 0
+
+    def __index__(self):
+        return 0
+
+    def __hash__(self):
+        return 0
+
+    def __eq__(self, o):
+        return False
+
+    def __bool__(self):
+        return False
+
+    def __len__(self):
+        return 0
+
+    def __getitem__(self, k):
+        return _Dummy()
+
+    def __mro_entries__(self, bases):
+        return (object,)
+
+    __add__ = __radd__ = __sub__ = __rsub__ = __mul__ = __rmul__ = __or__ = __ror__ = __and__ = __rand__ = \
+        __xor__ = __lshift__ = __rshift__ = __mod__ = __floordiv__ = __truediv__ = __neg__ = __invert__ = \
+        lambda self, *a: _Dummy()
+
+
+class _DummyModule(types.ModuleType):
+    def __getattr__(self, k):
+        if k.startswith("__"):
+            raise AttributeError(k)
+        return _Dummy()
+
+
+def install_chess_stand_in():
+    chess = _DummyModule("chess")
+    chess.__path__ = []
+    sys.modules["chess"] = chess
+    for sub in ("pgn", "engine", "polyglot", "svg"):
+        m = _DummyModule("chess." + sub)
+        sys.modules["chess." + sub] = m
+        setattr(chess, sub, m)
+
+
+def make_model(brain) -> dict:
+    import chessfly.model as M
+    import chessfly.selfplay as SP
+    import chessfly.train as TR
+    conn = synth.tiny(60, 600)
+    torch.manual_seed(0)
+    net = M.FlyChessNet(conn, M.ModelConfig(steps=3))
+    g = torch.Generator().manual_seed(5)
+    with torch.no_grad():
+        for layer in (net.policy, net.value, net.policy_from, net.policy_to):
+            layer.weight.copy_(torch.randn(layer.weight.shape, generator=g) * 0.05)
+            layer.bias.copy_(torch.randn(layer.bias.shape, generator=g) * 0.05)
+        net.brain.log_gain.add_(torch.randn(net.brain.log_gain.shape, generator=g) * 0.2)
+    rec = {"state_" + k: v.detach().numpy().copy() for k, v in net.state_dict().items()}
+    x = synth.boards(6, seed=1)
+    net.eval()
+    with torch.no_grad():
+        logits, wdl = net(torch.from_numpy(x))
+    rec.update(x=x, eval_logits=logits.numpy(), eval_wdl=wdl.numpy())
+    rng = np.random.default_rng(2)
+    batch, idxs, pis, qs, wdls = [], [], [], [], []
+    for i in range(8):
+        idx = np.sort(rng.choice(4168, 30, replace=False)).astype(np.int16)
+        z = rng.standard_normal(30)
+        pi = (np.exp(z) / np.exp(z).sum()).astype(np.float16)
+        q = float(rng.uniform(-1, 1))
+        w = int(rng.choice(3, p=[0.45, 0.10, 0.45]))
+        batch.append(SP.Sample(synth.boards(1, seed=10 + i)[0].astype(np.float16), idx, pi, q, w))
+        idxs.append(idx), pis.append(pi), qs.append(q), wdls.append(w)
+    rec.update(batch_x=np.stack([s.x for s in batch]), batch_idx=np.stack(idxs), batch_pi=np.stack(pis),
+               batch_q=np.array(qs), batch_wdl=np.array(wdls))
+    net.train()
+    opt = TR.make_optimizer(net, TR.TrainConfig())
+    res = TR.train_step(net, opt, batch, "cpu", q_ratio=0.5)
+    rec.update(train_policy_loss=res["policy_loss"], train_value_loss=res["value_loss"], train_value_ce=res["value_ce"])
+    for k, p in net.named_parameters():
+        rec["grad_" + k] = p.grad.detach().numpy().copy()
+        rec["after_" + k] = p.detach().numpy().copy()
+    rec["norm_mean"], rec["norm_var"] = net.norm.mean.numpy().copy(), net.norm.var.numpy().copy()
+    return rec
+
+
 def main():
     ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("ALPHAFLY_REFERENCE")
     if not ref:
         sys.exit("usage: make_golden.py /path/to/reference/checkout")
     sys.path.insert(0, ref)
-    sys.modules.setdefault("chess", types.ModuleType("chess"))
+    install_chess_stand_in()
     import chessfly.brain as brain
     torch.set_num_threads(os.cpu_count() or 1)
-    which = sys.argv[2:] or ["tiny", "small", "shuffled", "full"]
+    which = sys.argv[2:] or ["tiny", "small", "shuffled", "full", "model"]
     for name in which:
-        rec = {"tiny": make_tiny, "small": make_small, "shuffled": make_shuffled, "full": make_full}[name](brain)
+        rec = {"tiny": make_tiny, "small": make_small, "shuffled": make_shuffled, "full": make_full,
+               "model": make_model}[name](brain)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
         print(name, "written:", len(rec), "arrays")
 

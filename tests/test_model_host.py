@@ -1,0 +1,40 @@
+"""The model layer's host-side contract (chessfly/model.py): checkpoint keys identical to the reference's,
+load_weights' tolerance for old checkpoints, move squares.  No GPU needed (construction only)."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from alphafly_b200 import synth
+from alphafly_b200.encoding import N_BASE, N_FEATURES, N_MOVES, move_squares
+from alphafly_b200.model import FlyChessNet, ModelConfig, load_weights
+
+
+def test_state_dict_keys_and_shapes_match_the_reference():
+    g = golden("model")
+    ref = {k[len("state_"):]: g[k].shape for k in g.files if k.startswith("state_")}
+    net = FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3))
+    mine = {k: tuple(v.shape) for k, v in net.state_dict().items()}
+    assert mine == {k: tuple(v) for k, v in ref.items()}
+
+
+def test_constants_and_move_squares():
+    assert (N_BASE, N_FEATURES, N_MOVES) == (838, 967, 4168)
+    frm, to = move_squares()
+    assert frm.shape == to.shape == (N_MOVES,)
+    assert frm[64 * 12 + 28] == 12 and to[64 * 12 + 28] == 28
+    assert frm[4096] == 48 and to[4096] == 56 and to[4096 + 3] == 56 and to[4096 + 6] == 57
+    assert frm.max() < 64 and to.max() < 64
+
+
+def test_load_weights_accepts_old_checkpoints_and_rejects_incomplete_ones():
+    """tests/test_core.py:394-471: missing factorised heads load; a narrower encoder is zero-padded; a
+    genuinely missing tensor is an error."""
+    net = FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3))
+    old = {k: v.clone() for k, v in net.state_dict().items() if not k.startswith(("policy_from.", "policy_to."))}
+    old["encoder.weight"] = old["encoder.weight"][:, :N_BASE].clone()
+    load_weights(net, old)
+    assert float(net.encoder.weight[:, N_BASE:].abs().sum()) == 0
+    with pytest.raises(RuntimeError, match="does not match"):
+        load_weights(net, {k: v for k, v in old.items() if k != "value.bias"})
