@@ -18,6 +18,8 @@
 // row end.  Column indices and values are loaded 32 edges at a time, coalesced, and broadcast with
 // shuffles.
 // Accumulation is float32 in every mode.
+#include <cudaTypedefs.h>
+
 #include "internal.cuh"
 
 namespace afb {
@@ -359,6 +361,13 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
 
+// How a float16 row slice is multiplied into the float32 accumulators: 0 = mixed-precision
+// fma.rn.f32.f16, 1 = convert half2 -> float2 then fmaf, 2 = convert then packed fma.rn.f32x2.
+// All three round each product-sum once in float32 and give the same results.
+#ifndef AFB_HALF_MATH
+#define AFB_HALF_MATH 0
+#endif
+
 template <typename T>
 struct Gather;
 
@@ -370,6 +379,7 @@ struct Gather<__half> {
     __device__ static void fma(float (&acc)[8], uint32_t v, uint32_t addr) {
         uint32_t r[4];
         asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+#if AFB_HALF_MATH == 0
         const unsigned short vh = (unsigned short)v;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -378,6 +388,21 @@ struct Gather<__half> {
             asm("fma.rn.f32.f16 %0, %1, %2, %0;\n" : "+f"(acc[2 * k]) : "h"(lo), "h"(vh));
             asm("fma.rn.f32.f16 %0, %1, %2, %0;\n" : "+f"(acc[2 * k + 1]) : "h"(hi), "h"(vh));
         }
+#else
+        const float vf = __half2float(__ushort_as_half((unsigned short)v));
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&r[k]));
+#if AFB_HALF_MATH == 1
+            acc[2 * k] = fmaf(vf, f.x, acc[2 * k]);
+            acc[2 * k + 1] = fmaf(vf, f.y, acc[2 * k + 1]);
+#else
+            asm("{\n .reg .b64 a, x, v;\n mov.b64 a, {%0, %1};\n mov.b64 x, {%2, %3};\n mov.b64 v, {%4, %4};\n"
+                " fma.rn.f32x2 a, x, v, a;\n mov.b64 {%0, %1}, a;\n}\n"
+                : "+f"(acc[2 * k]), "+f"(acc[2 * k + 1]) : "f"(f.x), "f"(f.y), "f"(vf));
+#endif
+        }
+#endif
     }
 };
 
@@ -691,6 +716,10 @@ __global__ void __launch_bounds__(kAWarps * 32, AFB_ASYNC_MINBLOCKS) step_kernel
 #ifndef AFB_TMA_FENCE
 #define AFB_TMA_FENCE 1
 #endif
+#ifndef AFB_TMA_GATHER4
+#define AFB_TMA_GATHER4 1
+#endif
+static_assert(!AFB_TMA_GATHER4 || AFB_TMA_CHUNK == 4, "gather4 moves four edges per copy");
 constexpr int kTStages = AFB_TMA_STAGES;
 constexpr int kTChunk = AFB_TMA_CHUNK;
 constexpr int kTWarpRing = kTStages * kTChunk * kRowBytes;
@@ -725,11 +754,20 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void *src, uint32_t
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n"
                  ::"r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(pol) : "memory");
 }
+// Four rows (y0..y3) of the 2-D tensor map, each one box (a full row tile) wide, into 4 consecutive
+// 512-byte slots at dst (sm_100a tile::gather4; the box is one row high, x = 0).
+__device__ __forceinline__ void gather4_g2s(uint32_t dst, const CUtensorMap *map, int y0, int y1, int y2, int y3,
+                                            uint32_t bar, uint64_t pol) {
+    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
+                 " [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;\n"
+                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(0), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(bar),
+                 "l"(pol) : "memory");
+}
 __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
 __device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
 
 template <typename T, typename TV>
-__global__ void __launch_bounds__(kAWarps * 32, AFB_TMA_MINBLOCKS) step_kernel_tma(const StepArgs a) {
+__global__ void __launch_bounds__(kAWarps * 32, AFB_TMA_MINBLOCKS) step_kernel_tma(const __grid_constant__ StepArgs a) {
     using G = Gather<T>;
     constexpr int V = G::V;
     constexpr int BT = 32 * V;
@@ -804,16 +842,31 @@ __global__ void __launch_bounds__(kAWarps * 32, AFB_TMA_MINBLOCKS) step_kernel_t
             }
             const int n_valid = je - cs < kTChunk ? je - cs : kTChunk;
             const int stage = k % kTStages;
-#if AFB_TMA_ONE_LANE
+#if AFB_TMA_GATHER4
+            int cc[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) cc[u] = __shfl_sync(kFull, pcol, wo + (u < n_valid ? u : 0));
+            __syncwarp();
+            if (AFB_TMA_FENCE) fence_proxy_async_smem();
+            if (lane == 0) {
+                const int base = (int)(tile * a.rows_in);
+                mbar_arrive_expect_tx(bar_w + stage * 8, 4 * kRowBytes);
+                gather4_g2s(ring_w + stage * kTChunk * kRowBytes, &a.tmap, base + cc[0], base + cc[1], base + cc[2],
+                            base + cc[3], bar_w + stage * 8, keep);
+            }
+#elif AFB_TMA_ONE_LANE
             int cc[kTChunk];
 #pragma unroll
             for (int u = 0; u < kTChunk; ++u) cc[u] = __shfl_sync(kFull, pcol, wo + u);
 #else
             const int c = __shfl_sync(kFull, pcol, (wo + lane) & 31);
 #endif
+#if !AFB_TMA_GATHER4
             __syncwarp();
             if (AFB_TMA_FENCE) fence_proxy_async_smem();
-#if AFB_TMA_ONE_LANE
+#endif
+#if AFB_TMA_GATHER4
+#elif AFB_TMA_ONE_LANE
             if (lane == 0) {
                 mbar_arrive_expect_tx(bar_w + stage * 8, n_valid * kRowBytes);
 #pragma unroll
@@ -926,6 +979,28 @@ __global__ void __launch_bounds__(kAWarps * 32, AFB_TMA_MINBLOCKS) step_kernel_t
 #define AFB_ASYNC 1
 #endif
 
+// The gather kernel's tensor map of x_in: a 2-D tensor of tiles * rows_in rows, each one batch tile (bt
+// elements, 512 bytes) wide; the box is one row, so tile::gather4 fetches four arbitrary rows.
+void encode_gather_map(StepArgs &a, int elem_bytes, int bt, int64_t tiles) {
+    static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+    if (!encode) {
+        cudaDriverEntryPointQueryResult q;
+        void *fn = nullptr;
+        AFB_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+        AFB_CHECK(q == cudaDriverEntryPointSuccess && fn, "cuTensorMapEncodeTiled is not available from the driver");
+        encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    const cuuint64_t dim[2] = {(cuuint64_t)bt, (cuuint64_t)(tiles * a.rows_in)};
+    const cuuint64_t stride[1] = {(cuuint64_t)bt * elem_bytes};
+    const cuuint32_t box[2] = {(cuuint32_t)bt, 1};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = encode(&a.tmap, elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                              2, const_cast<void *>(a.x_in), dim, stride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AFB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
+}
+
 template <typename T, typename TV>
 void launch(const StepArgs &a, cudaStream_t s) {
     constexpr int BT = (AFB_ASYNC || AFB_TMA ? 32 : kLanesPerEdge) * Lane<T>::V;
@@ -934,6 +1009,8 @@ void launch(const StepArgs &a, cudaStream_t s) {
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
     if (AFB_TMA) {
+        StepArgs g = a;
+        if (AFB_TMA_GATHER4 && a.rows_in > 0) encode_gather_map(g, (int)sizeof(T), BT, tiles);
         static unsigned long long configured = 0;   // devices on which this instantiation may use kTRingBytes
         int dev = 0;
         AFB_CUDA(cudaGetDevice(&dev));
@@ -941,7 +1018,7 @@ void launch(const StepArgs &a, cudaStream_t s) {
             AFB_CUDA(cudaFuncSetAttribute(step_kernel_tma<T, TV>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTRingBytes));
             configured |= 1ull << dev;
         }
-        step_kernel_tma<T, TV><<<(unsigned)blocks, kAWarps * 32, kTRingBytes, s>>>(a);
+        step_kernel_tma<T, TV><<<(unsigned)blocks, kAWarps * 32, kTRingBytes, s>>>(g);
     } else if (AFB_ASYNC) {
         static unsigned long long configured = 0;   // devices on which this instantiation may use kRingBytes
         int dev = 0;

@@ -58,6 +58,17 @@ def peaks():
     return 6650.0, "fallback"
 
 
+def measured_traffic():
+    """Per-launch DRAM bytes of the step kernel from the committed ncu capture (profiles/), or None."""
+    path = os.path.join(HERE, "profiles", "step_kernel_traffic_config3.txt")
+    if not os.path.exists(path):
+        return None
+    for line in open(path):
+        if line.startswith("bytes_per_launch"):
+            return int(line.split("=")[1])
+    return None
+
+
 def workload(seed=0):
     from alphafly_b200 import synth
     return synth.full(seed)
@@ -258,7 +269,9 @@ def main():
     gathered = sum(cone.nnz) * B * 2                          # state bytes the SpMM pulls through L2 per forward
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
                 "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
-                "traffic": None, "kernel": "step_kernel<__half,__half> (6 launches per forward)",
+                "traffic": measured_traffic() if B == 35_840 else None,
+                "traffic_source": "profiles/step_kernel_traffic_config3.txt (ncu, B = 35,840)",
+                "kernel": "step_kernel_async<__half,__half> (6 launches per forward)",
                 "algorithmic_bytes_per_launch": int(sum(per_step_bytes) / STEPS_T),
                 "launch_ms": [round(x, 3) for x in kernel_ms],
                 "l2_gather_bytes_per_forward": int(gathered),
@@ -266,26 +279,54 @@ def main():
 
     e2e = None
     if not args.no_e2e:
+        # Through the public call with host buffers: each step copies its drive from pinned host memory and
+        # its output back, on a copy stream double-buffered against the compute stream (the reference's
+        # self-play pipelines its GPU rounds the same way, chessfly/workers.py:121-124,162-164).
         pin_u = u_host.pin_memory()
-        pin_out = torch.empty(len(inst.out_idx), B, dtype=torch.float32).pin_memory()
-        u_dev = torch.empty_like(u)
+        pin_out = [torch.empty(len(inst.out_idx), B, dtype=torch.float32).pin_memory() for _ in range(2)]
+        u_dev = [torch.empty_like(u), torch.empty_like(u)]
+        copy = torch.cuda.Stream(dev)
+        h2d_done = [torch.cuda.Event() for _ in range(2)]
+        out_ready = [torch.cuda.Event() for _ in range(2)]
+        d2h_done = [torch.cuda.Event() for _ in range(2)]
+
+        def run(k_steps):
+            outs = [None, None]
+            with torch.cuda.stream(copy):
+                u_dev[0].copy_(pin_u, non_blocking=True)
+                h2d_done[0].record(copy)
+            for k in range(k_steps):
+                i = k % 2
+                if k + 1 < k_steps:                       # prefetch the next step's drive
+                    with torch.cuda.stream(copy):
+                        if k >= 1:
+                            copy.wait_event(out_ready[(k + 1) % 2])   # its buffer's previous forward is done
+                        u_dev[(k + 1) % 2].copy_(pin_u, non_blocking=True)
+                        h2d_done[(k + 1) % 2].record(copy)
+                stream.wait_event(h2d_done[i])
+                if k >= 2:
+                    stream.wait_event(d2h_done[i])        # the pinned output buffer is free again
+                outs[i] = rnn.forward_io(u_dev[i], in_idx, out_idx, STEPS_T)
+                out_ready[i].record(stream)
+                with torch.cuda.stream(copy):
+                    copy.wait_event(out_ready[i])
+                    pin_out[i].copy_(outs[i], non_blocking=True)
+                    d2h_done[i].record(copy)
+            copy.synchronize()
+
         with torch.no_grad():
-            for _ in range(2):
-                u_dev.copy_(pin_u, non_blocking=True)
-                pin_out.copy_(rnn.forward_io(u_dev, in_idx, out_idx, STEPS_T), non_blocking=True)
+            run(2)
             barrier()
             s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s0.record(stream)
-            for _ in range(args.steps):
-                u_dev.copy_(pin_u, non_blocking=True)
-                pin_out.copy_(rnn.forward_io(u_dev, in_idx, out_idx, STEPS_T), non_blocking=True)
-            s1.record(stream)
+            run(args.steps)
+            s1.record(copy)
             barrier()
         e2e_ms = max_over_ranks(s0.elapsed_time(s1))
         e2e = {"value": world * B * args.steps / (e2e_ms / 1000.0), "unit": UNIT,
                "h2d_bytes_per_step": pin_u.numel() * pin_u.element_size(),
-               "d2h_bytes_per_step": pin_out.numel() * pin_out.element_size(),
-               "ms_per_step": e2e_ms / args.steps}
+               "d2h_bytes_per_step": pin_out[0].numel() * pin_out[0].element_size(),
+               "ms_per_step": e2e_ms / args.steps, "pipelined": "copy stream, double-buffered"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
