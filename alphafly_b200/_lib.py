@@ -26,7 +26,7 @@ _f = ctypes.c_float
 _sz = ctypes.c_size_t
 _pp = ctypes.POINTER(ctypes.c_void_p)
 
-# name -> (restype, argtypes); every entry point of include/afb.h
+# name -> (restype, argtypes); every entry point of include/afb.h and include/afb_probe.h
 SIGNATURES = {
     "afb_last_error": (ctypes.c_char_p, []),
     "afb_version": (_int, []),
@@ -52,6 +52,8 @@ SIGNATURES = {
     "afb_graph_destroy": (None, [_p]),
     "afb_graph_forward_workspace": (_sz, [_p, _i64]),
     "afb_graph_forward": (_int, [_p, _p, _p, _p, _f, _p, _i64, _i64, _int, _p, _i64, _p, _sz, _p]),
+    "afb_probe_gather_sink_words": (_i64, []),
+    "afb_probe_gather": (_int, [_int, _int, _p, _i64, _p, _i64, _p, _i64, _p]),
 }
 
 _lib = None

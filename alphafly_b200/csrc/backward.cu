@@ -254,7 +254,6 @@ int afb_cone_forward_train(const afb_cone *c, const float *u_in, int64_t ld_u, i
             a.rc = sp.rc[AFB_MODE_F32].get();
             a.x_in = x_in;
             a.ts_in = ts_in;
-            a.rows_in = c->st[t - 1].n_rows;
             a.u = u_in;
             a.ld_u = ld_u;
             a.u_vec_ok = u_vec_ok;

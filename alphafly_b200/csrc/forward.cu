@@ -260,7 +260,6 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
             a.n_items = sp.op.n_items;
             a.rc = sp.rc[mode].get();
             a.x_in = x_in ? x_in : buf[(t + 1) & 1];   // step 1 reads no state (R_0 is empty)
-            a.rows_in = c->st[t - 1].n_rows;
             a.ts_in = ts_in;
             a.u = u_in;
             a.ld_u = ld_u;
@@ -333,7 +332,6 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
             a.rc = t == 1 ? rc_first : rc_rest;
             a.x_in = x_in;
             a.ts_in = ts;
-            a.rows_in = t == 1 ? 0 : n;
             a.u = u;
             a.ld_u = ld_u;
             a.u_vec_ok = u_vec_ok;

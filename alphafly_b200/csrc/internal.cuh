@@ -1,8 +1,6 @@
 // Internal data structures shared by the library's translation units.
 #pragma once
 
-#include <cuda.h>
-
 #include "common.cuh"
 
 namespace afb {
@@ -51,9 +49,6 @@ struct Step {
 };
 
 // Compile-time tuning of the step kernel (defaults are the shipped configuration).
-#ifndef AFB_LPE
-#define AFB_LPE 16
-#endif
 #ifndef AFB_ITEM_COST
 #define AFB_ITEM_COST 4096
 #endif
@@ -86,8 +81,6 @@ struct StepArgs {
     int64_t batch;
     int *err;                      // device status word: set non-zero when a bounded wait gives up
     float *y_out;                  // training forward: pre-clamp drive of R_t, tile-major (float32 state only)
-    int64_t rows_in;               // |R_{t-1}|: rows of x_in per batch tile
-    CUtensorMap tmap;              // TMA gather kernel: x_in as a 2-D tensor (tiles * rows_in rows of one tile each)
 };
 
 // Batch columns one CTA covers for a state element of `elem_bytes`; the state's leading dimension is

@@ -69,6 +69,31 @@ def measured_traffic():
     return None
 
 
+def gather_ceiling(dev, slab_rows, n_rows=1 << 25, reps=5, path=0, blocks_per_sm=0):
+    """Device ceiling of the step kernel's dominant access: n_rows random 512-byte rows of a slab of
+    ``slab_rows`` rows gathered by the library's probe kernel through load path ``path`` (include/afb_probe.h;
+    0 = 16-byte loads into registers); GB/s (median of reps)."""
+    from alphafly_b200 import _lib
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(5)
+    slab = torch.randint(0, 1 << 30, (slab_rows, 128), dtype=torch.int32, device=dev, generator=g)
+    rows = torch.randint(0, slab_rows, (n_rows,), dtype=torch.int32, device=dev, generator=g)
+    words = lib.afb_probe_gather_sink_words()
+    sink = torch.empty(words, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    args = (path, blocks_per_sm, slab.data_ptr(), slab_rows, rows.data_ptr(), n_rows, sink.data_ptr(), words, stream.cuda_stream)
+    times = []
+    for k in range(3 + reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        _lib.check(lib.afb_probe_gather(*args))
+        b.record(stream)
+        b.synchronize()
+        if k >= 3:
+            times.append(a.elapsed_time(b))
+    return n_rows * 512 / (statistics.median(times) / 1000.0) / 1e9
+
+
 def workload(seed=0):
     from alphafly_b200 import synth
     return synth.full(seed)
@@ -271,11 +296,17 @@ def main():
                 "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                 "traffic": measured_traffic() if B == 35_840 else None,
                 "traffic_source": "profiles/step_kernel_traffic_config3.txt (ncu, B = 35,840)",
-                "kernel": "step_kernel_async<__half,__half> (6 launches per forward)",
+                "kernel": "step_kernel<__half,__half> (6 launches per forward)",
                 "algorithmic_bytes_per_launch": int(sum(per_step_bytes) / STEPS_T),
                 "launch_ms": [round(x, 3) for x in kernel_ms],
                 "l2_gather_bytes_per_forward": int(gathered),
                 "l2_gather_gbs": round(gathered / (kernel_total_ms / 1000.0) / 1e9, 1)}
+    # the same 512-byte-row gather alone, over a slab as large as the widest step's state tile
+    ceiling = gather_ceiling(dev, max(cone.rows_len))
+    roofline.update({"l2_gather_ceiling_gbs": round(ceiling, 1),
+                     "l2_gather_frac": round(roofline["l2_gather_gbs"] / ceiling, 4),
+                     "l2_gather_ceiling_source": "afb_probe_gather: 2^25 uniform random rows of a "
+                                                 f"{max(cone.rows_len):,} x 512 B slab, measured in this run"})
 
     e2e = None
     if not args.no_e2e:

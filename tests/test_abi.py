@@ -1,4 +1,4 @@
-"""The C ABI: every entry point declared in include/afb.h is exported by libafb.so and bound by the
+"""The C ABI: every entry point declared in include/*.h is exported by libafb.so and bound by the
 Python host, and argument errors come back as AfbError without touching a GPU."""
 
 import ctypes
@@ -11,7 +11,8 @@ from conftest import ROOT
 
 
 def declared():
-    text = open(os.path.join(ROOT, "include", "afb.h")).read()
+    inc = os.path.join(ROOT, "include")
+    text = "".join(open(os.path.join(inc, f)).read() for f in sorted(os.listdir(inc)) if f.endswith(".h"))
     return sorted(set(re.findall(r"AFB_API\s+[\w\s\*]*?\b(afb_\w+)\s*\(", text)))
 
 
