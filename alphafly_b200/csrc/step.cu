@@ -259,6 +259,7 @@ template <>
 struct Gather<__half> {
     static constexpr int V = 8;
     __device__ static uint32_t bits(const __half *p, uint64_t pol) { return ld_stream_b16(p, pol); }
+    __device__ static uint32_t bits_plain(const __half *p) { return __ldg(reinterpret_cast<const unsigned short *>(p)); }
     // acc[0..7] += v * x[0..7], x = the 8 float16 values at shared address addr
     __device__ static void fma(float (&acc)[8], uint32_t v, uint32_t addr) {
         uint4 x;
@@ -299,6 +300,7 @@ template <>
 struct Gather<float> {
     static constexpr int V = 4;
     __device__ static uint32_t bits(const float *p, uint64_t pol) { return ld_stream_b32(p, pol); }
+    __device__ static uint32_t bits_plain(const float *p) { return __ldg(reinterpret_cast<const unsigned *>(p)); }
     __device__ static void fma(float (&acc)[4], uint32_t v, uint32_t addr) {
         uint4 x;
         asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w) : "r"(addr));
@@ -601,6 +603,12 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_RING_MINBLOCKS) step_kernel_r
 #ifndef AFB_MINBLOCKS
 #define AFB_MINBLOCKS 5
 #endif
+#ifndef AFB_FULL_WINDOW
+#define AFB_FULL_WINDOW 1    // unpredicated path for the full chunks of a window
+#endif
+#ifndef AFB_GATHER_HINT
+#define AFB_GATHER_HINT 0    // 1: L2 evict-last on the gathered rows, evict-first on the indices and values
+#endif
 constexpr int kChunkR = AFB_CHUNK;
 
 // Per-warp loop bounds live in shared memory and are re-read where they are needed (volatile), so
@@ -669,14 +677,42 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
         for (int base = eb; base < ee; base += 32) {
             const int n = ee - base < 32 ? ee - base : 32;
             const int eoff = vld(s_e0) + base + lane;
-            const int my_col = lane < n ? __ldg(a.col + eoff) : 0;
-            const uint32_t my_val = lane < n ? G::bits(static_cast<const TV *>(a.val) + eoff, 0) : 0u;
-            for (int k = 0; k < n; k += kChunkR) {
+            int my_col = 0;
+            uint32_t my_val = 0u;
+            if (lane < n) {
+                if (AFB_GATHER_HINT) {
+                    const uint64_t once = policy_stream();
+                    my_col = (int)ld_stream_b32(a.col + eoff, once);
+                    my_val = G::bits(static_cast<const TV *>(a.val) + eoff, once);
+                } else {
+                    my_col = __ldg(a.col + eoff);
+                    my_val = G::bits_plain(static_cast<const TV *>(a.val) + eoff);
+                }
+            }
+            // full chunks: nothing predicated (chunks kept in sequence: one chunk's rows in registers at a time)
+            const int n_full = AFB_FULL_WINDOW ? n / kChunkR * kChunkR : 0;
+#pragma unroll 1
+            for (int k = 0; k < n_full; k += kChunkR) {
                 uint4 x[kChunkR];
+                const uint64_t keep = AFB_GATHER_HINT ? policy_keep() : 0;
+#pragma unroll
+                for (int u = 0; u < kChunkR; ++u) {
+                    const T *src = x_tile + __shfl_sync(kFull, my_col, k + u) * BT;
+                    x[u] = AFB_GATHER_HINT ? ld_stream_v4(src, keep) : __ldg(reinterpret_cast<const uint4 *>(src));
+                }
+#pragma unroll
+                for (int u = 0; u < kChunkR; ++u) G::fma(acc, __shfl_sync(kFull, my_val, k + u), x[u]);
+            }
+            // the window's last, partial chunk
+            for (int k = n_full; k < n; k += kChunkR) {
+                uint4 x[kChunkR];
+                const uint64_t keep = AFB_GATHER_HINT ? policy_keep() : 0;   // re-created per chunk: no live register
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) {
                     const int c = __shfl_sync(kFull, my_col, (k + u) & 31);
-                    x[u] = k + u < n ? __ldg(reinterpret_cast<const uint4 *>(x_tile + c * BT)) : make_uint4(0, 0, 0, 0);
+                    const T *src = x_tile + c * BT;
+                    x[u] = k + u >= n ? make_uint4(0, 0, 0, 0)
+                                      : AFB_GATHER_HINT ? ld_stream_v4(src, keep) : __ldg(reinterpret_cast<const uint4 *>(src));
                 }
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) G::fma(acc, __shfl_sync(kFull, my_val, (k + u) & 31), x[u]);
