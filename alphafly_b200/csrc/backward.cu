@@ -104,31 +104,73 @@ __global__ void bwd_rows(int n_rows, const RowConst *__restrict__ rc, const int 
 }
 
 // One warp per (row j of R_{t-1}, float32 batch tile of 128 columns; lane = 4 columns).
-__global__ void bwd_spmm_t(int n_cols, const int *__restrict__ t_crow, const int *__restrict__ t_col,
-                           const float *__restrict__ val_t, const float *__restrict__ gy, const float *__restrict__ gh,
-                           int64_t ts, const RowConst *__restrict__ rc, const int *__restrict__ inv,
-                           const float *__restrict__ h_prev, int64_t ts_prev, float *__restrict__ gh_prev,
-                           float *__restrict__ part, int64_t nnz) {
+// Sums of four values over the warp, reduce-scatter style: 6 shuffles instead of 4 x 5.  Lane 8 q ends
+// with the sum of v_q (q = 0..3); the addition order is fixed, so results are reproducible.
+__device__ __forceinline__ float warp_sum4(float v0, float v1, float v2, float v3, int lane) {
+    const bool h16 = lane & 16, h8 = lane & 8;
+    float k0 = h16 ? v2 : v0, k1 = h16 ? v3 : v1;
+    const float s0 = h16 ? v0 : v2, s1 = h16 ? v1 : v3;
+    k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+    k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+    float k = h8 ? k1 : k0;
+    k += __shfl_xor_sync(0xffffffffu, h8 ? k0 : k1, 8);
+    k += __shfl_xor_sync(0xffffffffu, k, 4);
+    k += __shfl_xor_sync(0xffffffffu, k, 2);
+    k += __shfl_xor_sync(0xffffffffu, k, 1);
+    return k;
+}
+
+// Transposed step of the backward, one warp per row j of R_{t-1} (taken longest first from `order`, so
+// that the longest rows do not finish last) and one 128-column float32 tile:
+//   g_prev[j] = sum_e w_e gy[post_e] + (1 - a_i) gh[i]      (i = the row of R_t carrying j, if any)
+//   part[tile][e] = sum over the tile's columns of h_prev[j] * gy[post_e]      (the SDDMM of dL/dw)
+// Column indices and values come 32 edges at a time (coalesced, broadcast with shuffles); the rows of gy
+// are gathered 4 edges at a time (4 loads in flight per lane), and the 4 edges' dot products are reduced
+// together (warp_sum4).
+__global__ void __launch_bounds__(256, 5) bwd_spmm_t(int n_cols, const int *__restrict__ order, const int *__restrict__ t_crow,
+                                                   const int *__restrict__ t_col,
+                                                   const float *__restrict__ val_t, const float *__restrict__ gy,
+                                                   const float *__restrict__ gh, int64_t ts, const RowConst *__restrict__ rc,
+                                                   const int *__restrict__ inv, const float *__restrict__ h_prev,
+                                                   int64_t ts_prev, float *__restrict__ gh_prev, float *__restrict__ part,
+                                                   int64_t nnz) {
     constexpr int bt = 128;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int j = blockIdx.x * (blockDim.x >> 5) + warp;
-    if (j >= n_cols) return;
+    const int jj = blockIdx.x * (blockDim.x >> 5) + warp;
+    if (jj >= n_cols) return;
+    const int j = __ldg(order + jj);
     const int64_t tile = blockIdx.y;
     const int off = lane * 4;
     const float4 hj = *reinterpret_cast<const float4 *>(h_prev + tile * ts_prev + (int64_t)j * bt + off);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     const float *gy_tile = gy + tile * ts + off;
-    const int e1 = t_crow[j + 1];
-    for (int e = t_crow[j]; e < e1; ++e) {
-        const int r = __ldg(t_col + e);
-        const float v = __ldg(val_t + e);
-        const float4 g = *reinterpret_cast<const float4 *>(gy_tile + (int64_t)r * bt);
-        acc.x = fmaf(v, g.x, acc.x);
-        acc.y = fmaf(v, g.y, acc.y);
-        acc.z = fmaf(v, g.z, acc.z);
-        acc.w = fmaf(v, g.w, acc.w);
-        const float d = warp_sum(g.x * hj.x + g.y * hj.y + g.z * hj.z + g.w * hj.w);
-        if (lane == 0) part[tile * nnz + e] = d;
+    float *part_tile = part + tile * nnz;
+    const int e0 = t_crow[j], e1 = t_crow[j + 1];
+    for (int base = e0; base < e1; base += 32) {
+        const int n = e1 - base < 32 ? e1 - base : 32;
+        const int my_r = lane < n ? __ldg(t_col + base + lane) : 0;
+        const float my_v = lane < n ? __ldg(val_t + base + lane) : 0.f;
+        for (int k = 0; k < n; k += 4) {
+            float4 g[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int r = __shfl_sync(0xffffffffu, my_r, (k + u) & 31);
+                g[u] = k + u < n ? *reinterpret_cast<const float4 *>(gy_tile + (int64_t)r * bt) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            float d[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const float v = __shfl_sync(0xffffffffu, my_v, (k + u) & 31);
+                acc.x = fmaf(v, g[u].x, acc.x);
+                acc.y = fmaf(v, g[u].y, acc.y);
+                acc.z = fmaf(v, g[u].z, acc.z);
+                acc.w = fmaf(v, g[u].w, acc.w);
+                d[u] = g[u].x * hj.x + g[u].y * hj.y + g[u].z * hj.z + g[u].w * hj.w;
+            }
+            const float s = warp_sum4(d[0], d[1], d[2], d[3], lane);
+            const int q = lane >> 3;
+            if ((lane & 7) == 0 && k + q < n) part_tile[base + k + q] = s;
+        }
     }
     const int i = inv[j];
     if (i >= 0) {
@@ -142,7 +184,6 @@ __global__ void bwd_spmm_t(int n_cols, const int *__restrict__ t_crow, const int
     *reinterpret_cast<float4 *>(gh_prev + tile * ts_prev + (int64_t)j * bt + off) = acc;
 }
 
-// dL/dw[edges[t_order[e]]] += sum over tiles of part[tile][e]   (the edges of one sub-matrix are distinct)
 __global__ void bwd_edge_sum(int64_t nnz, int64_t tiles, const float *__restrict__ part, const int *__restrict__ t_order,
                              const int *__restrict__ edges, float *__restrict__ g_w) {
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < nnz; e += (int64_t)gridDim.x * blockDim.x) {
@@ -350,7 +391,7 @@ int afb_cone_backward(const afb_cone *c, const float *g_out, int64_t ld_g, int64
             }
             if (m.present && pv.n_rows) {
                 dim3 grid((unsigned)((pv.n_rows + 7) / 8), (unsigned)tiles);
-                bwd_spmm_t<<<grid, kBlock, 0, s>>>(pv.n_rows, m.t_crow.get(), m.t_col.get(), sp.val32_t.get(), gy, g_here, ts,
+                bwd_spmm_t<<<grid, kBlock, 0, s>>>(pv.n_rows, m.t_heavy.get(), m.t_crow.get(), m.t_col.get(), sp.val32_t.get(), gy, g_here, ts,
                                                   sp.rc[AFB_MODE_F32].get(), sp.inv_prev.get(), h[t - 1], ts_prev, g_prev,
                                                   part, m.nnz);
                 AFB_LAUNCHED();

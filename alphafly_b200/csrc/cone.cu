@@ -112,6 +112,13 @@ __global__ void full_keys(const int *__restrict__ post, const int *__restrict__ 
 }
 
 // inv[prev[i]] = i for the carried rows i of R_t (prev is one-to-one onto its image)
+__global__ void row_lengths(const int *__restrict__ crow, int n, int *__restrict__ len, int *__restrict__ iota) {
+    for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < n; r += (int64_t)gridDim.x * blockDim.x) {
+        len[r] = crow[r + 1] - crow[r];
+        iota[r] = (int)r;
+    }
+}
+
 __global__ void invert_prev(const int *__restrict__ prev, int n_rows, int *__restrict__ inv) {
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_rows; i += gridDim.x * blockDim.x)
         if (prev[i] >= 0) inv[prev[i]] = i;
@@ -361,6 +368,18 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
             }
             crow_from_rows(m.post.get(), nnz, nr, m.crow, tmp, s);
             crow_from_rows(m.col.get(), nnz, nc, m.t_crow, tmp, s);
+            m.t_heavy.alloc(nc);
+            if (nc) {                          // rows of the transpose by decreasing length
+                DevBuf<int> len(nc), len_sorted(nc), iota(nc);
+                row_lengths<<<grid_for(nc, kBlock), kBlock, 0, s>>>(m.t_crow.get(), nc, len.get(), iota.get());
+                AFB_LAUNCHED();
+                size_t bytes = 0;
+                const int end_bit = bits_for((long long)nnz + 1);
+                AFB_CUDA(cub::DeviceRadixSort::SortPairsDescending(nullptr, bytes, len.get(), len_sorted.get(), iota.get(),
+                                                                   m.t_heavy.get(), nc, 0, end_bit, s));
+                AFB_CUDA(cub::DeviceRadixSort::SortPairsDescending(tmp.need(bytes), bytes, len.get(), len_sorted.get(), iota.get(),
+                                                                   m.t_heavy.get(), nc, 0, end_bit, s));
+            }
             build_schedule(m, s);
             c->edge_visits += m.present ? nnz : 0;
         }

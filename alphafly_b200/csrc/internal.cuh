@@ -26,6 +26,7 @@ struct Csr {
     DevBuf<int> crow, col;         // crow (n_rows + 1), col (nnz): local column index
     DevBuf<int> edges, post;       // edges (nnz): index into W's edge list; post (nnz): local row
     DevBuf<int> t_crow, t_col, t_order;  // CSR of the transpose, and the edge permutation into it
+    DevBuf<int> t_heavy;           // (n_cols) rows of the transpose, longest first (backward launch order)
     // schedule: contiguous row ranges ("items") of similar cost, launched heaviest first
     int n_items = 0;
     DevBuf<int> item_rows;         // (n_items + 1) row boundaries
