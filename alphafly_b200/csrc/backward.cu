@@ -69,28 +69,46 @@ __global__ void bwd_out(int n_out, const int *__restrict__ out_row, const int *_
 
 // One warp per row of R_t (see the file comment).
 __global__ void bwd_rows(int n_rows, const RowConst *__restrict__ rc, const int *__restrict__ rows, int64_t batch,
-                         int64_t cols, int bt, const float *__restrict__ gh, const float *__restrict__ y, int64_t ts,
+                         int64_t cols, const float *__restrict__ gh, const float *__restrict__ y, int64_t ts,
                          const float *__restrict__ h_prev, int64_t ts_prev, float *__restrict__ gy,
                          float *__restrict__ g_alpha, float *__restrict__ gc_prev, float *__restrict__ g_k,
-                         float *__restrict__ g_u, int64_t ld_gu) {
+                         float *__restrict__ g_u, int64_t ld_gu, int gu_vec) {
+    constexpr int bt = 128;                      // float32 batch tile: one float4 per lane
     const int lane = threadIdx.x & 31;
     for (int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < n_rows; r += (gridDim.x * blockDim.x) >> 5) {
         const RowConst q = rc[r];
         float s_alpha = 0.f, s_k = 0.f, s_pc = 0.f;
-        for (int64_t c = lane; c < cols; c += 32) {
-            const int64_t at = (c / bt) * ts + (int64_t)r * bt + c % bt;
-            float g_y = 0.f;
-            if (c < batch) {
-                const float g = gh[at], yv = y[at];
-                const float p = q.prev >= 0 ? h_prev[(c / bt) * ts_prev + (int64_t)q.prev * bt + c % bt] : q.pc;
-                const float x = fminf(fmaxf(yv, q.lo), q.hi) + q.e;
-                g_y = (yv >= q.lo && yv <= q.hi) ? q.a * g : 0.f;
-                s_alpha += g * (x - p);
-                s_k += g_y;
-                s_pc += (1.f - q.a) * g;
-                if (q.usrc >= 0) g_u[(int64_t)q.usrc * ld_gu + c] += g_y;
+        for (int64_t c0 = lane * 4; c0 < cols; c0 += bt) {
+            const int64_t tile = c0 / bt, at = tile * ts + (int64_t)r * bt + lane * 4;
+            const float4 g4 = *reinterpret_cast<const float4 *>(gh + at), y4 = *reinterpret_cast<const float4 *>(y + at);
+            const float4 p4 = q.prev >= 0 ? *reinterpret_cast<const float4 *>(h_prev + tile * ts_prev + (int64_t)q.prev * bt + lane * 4)
+                                          : make_float4(q.pc, q.pc, q.pc, q.pc);
+            const float g[4] = {g4.x, g4.y, g4.z, g4.w}, yv[4] = {y4.x, y4.y, y4.z, y4.w}, p[4] = {p4.x, p4.y, p4.z, p4.w};
+            float g_y[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                g_y[k] = 0.f;
+                if (c0 + k < batch) {
+                    const float x = fminf(fmaxf(yv[k], q.lo), q.hi) + q.e;
+                    g_y[k] = (yv[k] >= q.lo && yv[k] <= q.hi) ? q.a * g[k] : 0.f;
+                    s_alpha += g[k] * (x - p[k]);
+                    s_k += g_y[k];
+                    s_pc += (1.f - q.a) * g[k];
+                }
             }
-            gy[at] = g_y;
+            *reinterpret_cast<float4 *>(gy + at) = make_float4(g_y[0], g_y[1], g_y[2], g_y[3]);
+            if (q.usrc >= 0) {
+                float *gu = g_u + (int64_t)q.usrc * ld_gu + c0;
+                if (gu_vec && c0 + 4 <= batch) {
+                    float4 v = *reinterpret_cast<float4 *>(gu);
+                    v.x += g_y[0]; v.y += g_y[1]; v.z += g_y[2]; v.w += g_y[3];
+                    *reinterpret_cast<float4 *>(gu) = v;
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        if (c0 + k < batch) gu[k] += g_y[k];
+                }
+            }
         }
         s_alpha = warp_sum(s_alpha);
         s_k = warp_sum(s_k);
@@ -336,6 +354,8 @@ int afb_cone_backward(const afb_cone *c, const float *g_out, int64_t ld_g, int64
         const int64_t n = c->n, e = c->e, T = c->steps;
         const int64_t ld = padded_ld(batch, 4), bt = tile_cols(4), tiles = ld / bt;
         AFB_CHECK(bt == 128, "the backward kernels assume 128-column float32 tiles");
+        const int gu_vec = ld_gu % 4 == 0 && reinterpret_cast<uintptr_t>(g_u_in) % 16 == 0;
+        AFB_CHECK(bt == 128, "the backward kernels assume 128-column float32 tiles");
         char *ws = static_cast<char *>(workspace);
         const size_t state_b = align256((size_t)c->max_rows * ld * 4);
         float *gh[2] = {reinterpret_cast<float *>(ws), reinterpret_cast<float *>(ws + state_b)};
@@ -385,8 +405,8 @@ int afb_cone_backward(const afb_cone *c, const float *g_out, int64_t ld_g, int64
             const float *c_prev = c->resting.get() + (t - 1) * n;
             if (sp.n_rows) {
                 bwd_rows<<<grid_for((int64_t)sp.n_rows * 32, kBlock, 148 * 64), kBlock, 0, s>>>(
-                    sp.n_rows, sp.rc[AFB_MODE_F32].get(), sp.rows.get(), batch, ld, (int)bt, g_here, y[t], ts,
-                    t > 1 ? h[t - 1] : nullptr, ts_prev, gy, g_alpha, gc + (t - 1) * n, g_k, g_u_in, ld_gu);
+                    sp.n_rows, sp.rc[AFB_MODE_F32].get(), sp.rows.get(), batch, ld, g_here, y[t], ts,
+                    t > 1 ? h[t - 1] : nullptr, ts_prev, gy, g_alpha, gc + (t - 1) * n, g_k, g_u_in, ld_gu, gu_vec);
                 AFB_LAUNCHED();
             }
             if (m.present && pv.n_rows) {
