@@ -13,6 +13,8 @@ the drive in pinned host memory and the output copied back inside the timed regi
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the float32 port in
 oracle/, all host threads) on a bounded sample of the same workload and prints the same line.
+``--train`` times configuration 5 instead (FlyChessNet train_step, B = 2,048 per GPU, data parallel over
+NCCL under torchrun); ``--probe`` prints the device's gather ceiling for each load path.
 """
 
 from __future__ import annotations
@@ -47,7 +49,13 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    return ap.parse_args()
+    ap.add_argument("--train", action="store_true",
+                    help="time the training step instead (configuration 5: FlyChessNet train_step, B = 2,048 per GPU)")
+    ap.add_argument("--probe", action="store_true", help="print the gather ceiling of every load path and exit")
+    args = ap.parse_args()
+    if args.train and args.batch == 35_840:
+        args.batch = 2048
+    return args
 
 
 def peaks():
@@ -228,11 +236,115 @@ def reference_arm(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def probe_arm(args):
+    """Gather ceiling of each load path of include/afb_probe.h on configuration 3's widest slab, and of the
+    register path against warps per SM."""
+    dev = torch.device("cuda", 0)
+    rows = 166_688
+    names = {0: "ldg x8", 1: "cp.async", 2: "cp.async + read-back", 3: "tma gather4", 4: "tma gather4 + read-back",
+             5: "ldg x4", 6: "ldg x16"}
+    for path in (0, 1, 2, 3, 4):
+        print(json.dumps({"probe": names[path], "slab_rows": rows, "gbs": round(gather_ceiling(dev, rows, path=path), 1)}),
+              flush=True)
+    for path in (5, 0, 6):
+        for bps in (2, 3, 4, 5, 6, 8):
+            print(json.dumps({"probe": names[path], "warps_per_sm": 8 * bps, "slab_rows": rows,
+                              "gbs": round(gather_ceiling(dev, rows, path=path, blocks_per_sm=bps), 1)}), flush=True)
+
+
+def train_batch(inst, batch, seed):
+    """Configuration 5's synthetic batch: boards, policy targets softmax(N(0, 1)) over ~30 random legal moves,
+    WDL one-hots drawn 0.45 / 0.10 / 0.45, q uniform in [-1, 1]; as device tensors (x, pi, legal, wdl, q)."""
+    from alphafly_b200 import synth
+    from alphafly_b200.encoding import N_MOVES
+    rng = np.random.default_rng(seed)
+    x = synth.boards(batch, seed)
+    legal = np.zeros((batch, N_MOVES), bool)
+    pi = np.zeros((batch, N_MOVES), np.float32)
+    for b in range(batch):
+        idx = rng.choice(N_MOVES, size=30, replace=False)
+        z = np.exp(rng.standard_normal(30))
+        legal[b, idx] = True
+        pi[b, idx] = z / z.sum()
+    wdl = rng.choice(3, size=batch, p=[0.45, 0.10, 0.45])
+    q = rng.uniform(-1, 1, batch).astype(np.float32)
+    return tuple(torch.from_numpy(a).pin_memory() for a in (x, pi, legal, wdl, q))
+
+
+def train_arm(args, rank, world, local):
+    """Configuration 5: one FlyChessNet train_step (forward through the light cone, backward, gradient clip,
+    AdamW; with N GPUs the gradients are averaged over NCCL) per step on B positions per GPU."""
+    from alphafly_b200 import synth
+    from alphafly_b200.model import FlyChessNet, ModelConfig
+    from alphafly_b200.train import TrainConfig, attach_data_parallel, make_optimizer, train_step
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    inst = workload()
+    net = FlyChessNet(inst.conn, ModelConfig(steps=STEPS_T))
+    synth.apply(net.brain, inst)
+    w, b = synth.encoder_weights(len(inst.in_idx))
+    with torch.no_grad():
+        net.encoder.weight.copy_(torch.from_numpy(w))
+        net.encoder.bias.copy_(torch.from_numpy(b))
+        for k, v in synth.head_weights(len(inst.out_idx)).items():
+            dict(net.named_parameters())[k].copy_(torch.from_numpy(v))
+    net = net.to(dev).train()
+    if world > 1:
+        attach_data_parallel(net)
+    opt = make_optimizer(net, TrainConfig())
+    host = train_batch(inst, args.batch, seed=77 + rank)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        batch = tuple(t.to(dev, non_blocking=True) for t in host)    # the batch arrives from pinned host memory
+        return train_step(net, opt, batch, dev, q_ratio=0.5, data_parallel=world > 1)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            res = step()
+        stop.record(stream)
+        barrier()
+    ms = start.elapsed_time(stop)
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    ms = float(t.item())
+    value = world * args.batch * args.steps / (ms / 1000.0)
+    if rank == 0:
+        h2d = sum(a.numel() * a.element_size() for a in host)
+        print(json.dumps({"metric": "connectome training positions/sec (6-step light-cone forward + backward + AdamW)",
+                          "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "f32", "data": "synthetic",
+                          "config": {"workload": "config5: FlyChessNet train_step on the full-scale synthetic connectome",
+                                     "positions_per_gpu": args.batch, "global_positions": args.batch * world,
+                                     "parallelism": f"data parallel over {world} GPU(s), NCCL gradient all-reduce"},
+                          "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 12,
+                                  "note": "the timed steps include the batch copy from pinned memory and the loss read-back"},
+                          "last_losses": res, "clocks": clocks.summary()}), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     args = parse()
     rank, world, local = init_dist(args)
     if args.impl == "reference":
         return reference_arm(args, rank, world)
+    if args.probe:
+        return probe_arm(args)
+    if args.train:
+        return train_arm(args, rank, world, local)
     from alphafly_b200 import synth
     from alphafly_b200.brain import ConnectomeRNN
     dev = torch.device("cuda", local)
