@@ -75,6 +75,19 @@ struct Lane<__half> {
 // p = previous state (or the constant pc), out = p + a (x - p); written to the tile-major x_out (and
 // y to y_out in the training forward).  The previous state and the drive are kept packed and converted
 // a pair at a time, to keep few registers live.
+// One-pass traffic (sub-matrix indices and values, the input drive, the new state) can be marked
+// streaming (ld/st .cs: evict first), leaving L2 to the gathered slab.
+#ifndef AFB_STREAM_CS
+#define AFB_STREAM_CS 0
+#endif
+template <typename X>
+__device__ __forceinline__ X ld_once(const X *p) { return AFB_STREAM_CS ? __ldcs(p) : __ldg(p); }
+template <typename X>
+__device__ __forceinline__ void st_once(X *p, const X &v) {
+    if (AFB_STREAM_CS) __stcs(p, v);
+    else *p = v;
+}
+
 template <typename T, int BT>
 __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t tile, int off, const float (&acc)[Lane<T>::V]) {
     constexpr int V = Lane<T>::V;
@@ -85,7 +98,7 @@ __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t t
     uint4 up = make_uint4(0, 0, 0, 0), pp = make_uint4(0, 0, 0, 0);
     const T *u = static_cast<const T *>(a.u) + (int64_t)(usrc >= 0 ? usrc : 0) * a.ld_u + col0;
     const bool u_vec = usrc >= 0 && a.u_vec_ok && col0 + V <= a.batch;
-    if (u_vec) up = __ldg(reinterpret_cast<const uint4 *>(u));
+    if (u_vec) up = ld_once(reinterpret_cast<const uint4 *>(u));
     if (prev >= 0) pp = __ldg(reinterpret_cast<const uint4 *>(static_cast<const T *>(a.x_in) + tile * a.ts_in + (int64_t)prev * BT + off));
     const float kk = __int_as_float(w0.x), lo = __int_as_float(w0.y), hi = __int_as_float(w0.z), e = __int_as_float(w0.w);
     const float pc = __int_as_float(w1.x), al = __int_as_float(w1.y);
@@ -121,11 +134,11 @@ __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t t
             yr[k] = __float_as_uint(y[0]);
         }
     }
-    *reinterpret_cast<uint4 *>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off) =
-        make_uint4(outr[0], outr[1], outr[2], outr[3]);
+    st_once(reinterpret_cast<uint4 *>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off),
+            make_uint4(outr[0], outr[1], outr[2], outr[3]));
     if constexpr (sizeof(T) == 4)
         if (a.y_out)
-            *reinterpret_cast<uint4 *>(a.y_out + tile * a.ts_out + (int64_t)row * BT + off) = make_uint4(yr[0], yr[1], yr[2], yr[3]);
+            st_once(reinterpret_cast<uint4 *>(a.y_out + tile * a.ts_out + (int64_t)row * BT + off), make_uint4(yr[0], yr[1], yr[2], yr[3]));
 }
 
 __global__ void output_kernel(int n_out, const int *__restrict__ src, const float *__restrict__ base, int add_base,
@@ -259,7 +272,7 @@ template <>
 struct Gather<__half> {
     static constexpr int V = 8;
     __device__ static uint32_t bits(const __half *p, uint64_t pol) { return ld_stream_b16(p, pol); }
-    __device__ static uint32_t bits_plain(const __half *p) { return __ldg(reinterpret_cast<const unsigned short *>(p)); }
+    __device__ static uint32_t bits_plain(const __half *p) { return ld_once(reinterpret_cast<const unsigned short *>(p)); }
     // acc[0..7] += v * x[0..7], x = the 8 float16 values at shared address addr
     __device__ static void fma(float (&acc)[8], uint32_t v, uint32_t addr) {
         uint4 x;
@@ -300,7 +313,7 @@ template <>
 struct Gather<float> {
     static constexpr int V = 4;
     __device__ static uint32_t bits(const float *p, uint64_t pol) { return ld_stream_b32(p, pol); }
-    __device__ static uint32_t bits_plain(const float *p) { return __ldg(reinterpret_cast<const unsigned *>(p)); }
+    __device__ static uint32_t bits_plain(const float *p) { return ld_once(reinterpret_cast<const unsigned *>(p)); }
     __device__ static void fma(float (&acc)[4], uint32_t v, uint32_t addr) {
         uint4 x;
         asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w) : "r"(addr));
@@ -685,7 +698,7 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
                     my_col = (int)ld_stream_b32(a.col + eoff, once);
                     my_val = G::bits(static_cast<const TV *>(a.val) + eoff, once);
                 } else {
-                    my_col = __ldg(a.col + eoff);
+                    my_col = ld_once(a.col + eoff);
                     my_val = G::bits_plain(static_cast<const TV *>(a.val) + eoff);
                 }
             }
