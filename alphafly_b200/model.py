@@ -14,10 +14,13 @@ transpose copy.
 from __future__ import annotations
 
 import dataclasses
+from collections import OrderedDict
 
+import numpy as np
 import torch
 from torch import nn
 
+from . import _lib
 from .brain import ConnectomeRNN
 from .connectome import Connectome
 from .encoding import N_BASE, N_FEATURES, N_MOVES, move_squares
@@ -96,11 +99,16 @@ class FlyChessNet(nn.Module):
         u = torch.addmm(b.unsqueeze(1), w, x[:, :k].T, beta=g, alpha=g)
         return u.to(dtype).contiguous()
 
-    def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """x: (B, N_FEATURES) -> policy logits (B, N_MOVES), WDL logits (B, 3)."""
+    def readout(self, x: torch.Tensor) -> torch.Tensor:
+        """x: (B, N_FEATURES) -> the normalised output-neuron state r (B, len(out_idx)) the heads read
+        (chessfly/model.py:97-103)."""
         dtype = self.infer_dtype if x.is_cuda and not torch.is_grad_enabled() else torch.float32
         u_in = self.drive(x.float(), dtype)
-        r = self.norm(self.brain.forward_io(u_in, self.in_idx, self.out_idx, self.cfg.steps).T.float())
+        return self.norm(self.brain.forward_io(u_in, self.in_idx, self.out_idx, self.cfg.steps).T.float())
+
+    def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """x: (B, N_FEATURES) -> policy logits (B, N_MOVES), WDL logits (B, 3)."""
+        r = self.readout(x)
         logits = self.policy(r) + self.policy_from(r)[:, self.move_from] + self.policy_to(r)[:, self.move_to]
         return logits, self.value(r)
 
@@ -110,30 +118,165 @@ class FlyChessNet(nn.Module):
         return p[..., 0] - p[..., 2]
 
 
-class Evaluator:
-    """The ``evaluate`` callable of the search: numpy in, numpy out (chessfly/model.py:113-135).  Legal-move
-    logits are gathered on the GPU, so only those leave the card."""
+class _Handle:
+    """One submitted evaluation: its device results, the pinned buffers they are copied into, and the event
+    that marks the copies done.  ``get`` waits once and keeps the host arrays."""
 
-    def __init__(self, net: FlyChessNet, device):
-        self.net, self.device = net, device
+    def __init__(self, event, n_out, n_val, out_host, val_host, lazy):
+        self.event, self.n_out, self.n_val, self.out_host, self.val_host, self.lazy = event, n_out, n_val, out_host, val_host, lazy
+        self.value = None
+
+    def get(self):
+        if self.value is None:
+            self.event.synchronize()
+            out = self.out_host[:self.n_out].numpy().copy()
+            self.value = (out.reshape(self.n_val, N_MOVES) if self.lazy else out, self.val_host[:self.n_val].numpy().copy())
+            self.out_host = self.val_host = None
+        return self.value
+
+
+class Evaluator:
+    """The ``evaluate`` callable of the search: numpy in, numpy out (chessfly/model.py:113-135): ``submit``
+    launches an evaluation and returns at once, ``result`` waits for it; legal-move logits (float32) when
+    ``rows``/``cols`` are given, else the whole policy (float16, the lazy search), and the values.
+
+    The B200 pipeline behind the same contract:
+      - features, legal indices and results go through pinned host buffers, two sets used in turn, so
+        the copies are asynchronous and a round can be submitted while the previous one runs (the
+        self-play loop keeps one round in flight, chessfly/workers.py:118-167);
+      - with ``graphs`` the network up to its readout, values and from/to terms runs as one CUDA graph,
+        captured once per batch bucket (multiples of 256 positions, the step kernel's batch tile; at most
+        ``max_graphs`` kept); the weight-dependent constants are refreshed before a replay when a
+        parameter changed, so training between rounds is seen;
+      - legal-move logits come from ``afb_legal_logits``: only the requested dot products, instead of the
+        dense (B, 4168) product and a gather.
+    """
+
+    BUCKET = 256
+
+    def __init__(self, net: FlyChessNet, device, graphs: bool = True, max_graphs: int = 4):
+        self.net, self.device = net, torch.device(device)
+        self.graphs = graphs and self.device.type == "cuda"
+        self.max_graphs = max_graphs
+        self._graphs: "OrderedDict[int, tuple]" = OrderedDict()
+        self._slots = [dict(), dict()]
+        self._pending: list = [None, None]
+        self._turn = 0
+
+    # -- pinned staging --------------------------------------------------------------------------------
+    def _pinned(self, slot: int, name: str, n: int, dtype) -> torch.Tensor:
+        buf = self._slots[slot].get(name)
+        if buf is None or buf.numel() < n:
+            buf = torch.empty(max(n, 1024), dtype=dtype)
+            if self.device.type == "cuda":
+                buf = buf.pin_memory()
+            self._slots[slot][name] = buf
+        return buf
+
+    def _stage(self, slot: int, name: str, a: np.ndarray, dtype) -> torch.Tensor:
+        """``a`` copied into this slot's pinned buffer and sent to the device (asynchronously)."""
+        flat = np.ascontiguousarray(a).reshape(-1)
+        buf = self._pinned(slot, name, flat.size, dtype)
+        buf[:flat.size].numpy()[:] = flat
+        return buf[:flat.size].to(self.device, non_blocking=True)
+
+    # -- the network -------------------------------------------------------------------------------------
+    def _trunk(self, x: torch.Tensor):
+        net = self.net
+        r = net.readout(x)
+        return r, net.policy_from(r), net.policy_to(r), net.expected_value(net.value(r).float())
+
+    def _refresh_constants(self) -> None:
+        net, brain = self.net, self.net.brain
+        mode = _lib.MODE_DEV16 if net.infer_dtype == torch.float16 else _lib.MODE_F32
+        cone = brain.light_cone(net.in_idx, net.out_idx, net.cfg.steps)
+        cone.set_weights(brain, mode, brain._weight_key(mode, cone))
+
+    def _graph(self, bucket: int):
+        key = (bucket, self.net.infer_dtype)
+        entry = self._graphs.get(key)
+        if entry is not None:
+            self._graphs.move_to_end(key)
+            return entry
+        while len(self._graphs) >= self.max_graphs:
+            self._graphs.popitem(last=False)
+        x = torch.zeros(bucket, N_FEATURES, dtype=torch.float16, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):                  # warm-up: cone, constants, library handles
+            for _ in range(2):
+                self._trunk(x)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs = self._trunk(x)
+        entry = (g, x, outs)
+        self._graphs[key] = entry
+        return entry
 
     @torch.no_grad()
     def submit(self, x, rows, cols):
         """Launch the evaluation and return at once; ``result`` waits for it."""
-        self.net.eval()
-        logits, wdl = self.net(torch.from_numpy(x).to(self.device, non_blocking=True).float())
+        net = self.net
+        net.eval()
+        slot = self._turn
+        self._turn ^= 1
+        if self._pending[slot] is not None:            # its pinned buffers are about to be reused
+            self._pending[slot].get()
+        b = len(x)
+        if b == 0:
+            handle = _Handle(_Done(), 0, 0, torch.empty(0, dtype=torch.float16 if rows is None else torch.float32),
+                             torch.empty(0), rows is None)
+            self._pending[slot] = handle
+            return handle
+        x_dev = self._stage(slot, "x", np.asarray(x, np.float16), torch.float16).view(b, -1)
+        if self.graphs and x_dev.is_cuda and b > 0:
+            self._refresh_constants()
+            g, x_static, (r, f, t, values) = self._graph((b + self.BUCKET - 1) // self.BUCKET * self.BUCKET)
+            x_static[:b].copy_(x_dev)
+            g.replay()
+            r, f, t, values = r[:b], f[:b], t[:b], values[:b]
+        else:
+            r, f, t, values = self._trunk(x_dev)
         if rows is None:
-            return logits.half(), self.net.expected_value(wdl.float())
-        legal = logits[torch.from_numpy(rows).to(self.device, non_blocking=True),
-                       torch.from_numpy(cols).to(self.device, non_blocking=True)]
-        return legal.float(), self.net.expected_value(wdl.float())
+            out = (net.policy(r) + f[:, net.move_from] + t[:, net.move_to]).half().reshape(-1)
+        else:
+            rows_dev = self._stage(slot, "rows", np.asarray(rows, np.int64), torch.int64)
+            cols_dev = self._stage(slot, "cols", np.asarray(cols, np.int64), torch.int64)
+            out = torch.empty(len(rows_dev), dtype=torch.float32, device=self.device)
+            if out.is_cuda:
+                lib = _lib.load()
+                w, bias = net.policy.weight.detach(), net.policy.bias.detach()
+                _lib.check(lib.afb_legal_logits(len(out), rows_dev.data_ptr(), cols_dev.data_ptr(), b, r.shape[1],
+                                                r.contiguous().data_ptr(), w.shape[0], w.contiguous().data_ptr(),
+                                                bias.data_ptr(), f.shape[1], f.contiguous().data_ptr(),
+                                                t.contiguous().data_ptr(), net.move_from.data_ptr(),
+                                                net.move_to.data_ptr(), out.data_ptr(),
+                                                torch.cuda.current_stream(self.device).cuda_stream))
+            else:
+                out = (net.policy(r) + f[:, net.move_from] + t[:, net.move_to])[rows_dev, cols_dev]
+        out_host = self._pinned(slot, "out_half" if rows is None else "out", out.numel(), out.dtype)
+        val_host = self._pinned(slot, "values", b, torch.float32)
+        out_host[:out.numel()].copy_(out, non_blocking=True)
+        val_host[:b].copy_(values.float(), non_blocking=True)
+        ev = torch.cuda.Event() if out.is_cuda else None
+        if ev is not None:
+            ev.record(torch.cuda.current_stream(self.device))
+        handle = _Handle(ev if ev is not None else _Done(), out.numel(), b, out_host, val_host, rows is None)
+        self._pending[slot] = handle
+        return handle
 
-    @staticmethod
-    def result(handle):
-        return handle[0].cpu().numpy(), handle[1].float().cpu().numpy()
+    def result(self, handle):
+        return handle.get()
 
     def __call__(self, x, rows, cols):
         return self.result(self.submit(x, rows, cols))
+
+
+class _Done:
+    @staticmethod
+    def synchronize():
+        pass
 
 
 NEW_HEADS = ("policy_from.", "policy_to.")

@@ -14,7 +14,8 @@ the drive in pinned host memory and the output copied back inside the timed regi
 ``--impl reference`` times the reference algorithm's CPU implementation (the float32 port in
 oracle/, all host threads) on a bounded sample of the same workload and prints the same line.
 ``--train`` times configuration 5 instead (FlyChessNet train_step, B = 2,048 per GPU, data parallel over
-NCCL under torchrun); ``--probe`` prints the device's gather ceiling for each load path.
+NCCL under torchrun); ``--probe`` prints the device's gather ceiling for each load path; ``--evaluator``
+times self-play evaluation rounds (B = 1,120 positions) through three implementations of the Evaluator.
 """
 
 from __future__ import annotations
@@ -52,9 +53,13 @@ def parse():
     ap.add_argument("--train", action="store_true",
                     help="time the training step instead (configuration 5: FlyChessNet train_step, B = 2,048 per GPU)")
     ap.add_argument("--probe", action="store_true", help="print the gather ceiling of every load path and exit")
+    ap.add_argument("--evaluator", action="store_true",
+                    help="time the self-play Evaluator (FlyChessNet rounds of --batch positions, 30 legal moves each)")
     args = ap.parse_args()
     if args.train and args.batch == 35_840:
         args.batch = 2048
+    if args.evaluator and args.batch == 35_840:
+        args.batch = 1120
     return args
 
 
@@ -336,6 +341,69 @@ def train_arm(args, rank, world, local):
         torch.distributed.destroy_process_group()
 
 
+def evaluator_arm(args):
+    """Self-play evaluation rounds (chessfly/workers.py:118-167): B positions per round with 30 legal moves
+    each, one round in flight while the next is submitted.  Three implementations of the same contract:
+    the reference's eager Evaluator logic (dense logits, gather, blocking copies), and this package's
+    Evaluator without and with CUDA graphs (pinned staging, fused legal-move logits)."""
+    from alphafly_b200 import synth
+    from alphafly_b200.model import Evaluator, FlyChessNet, ModelConfig
+    dev = torch.device("cuda", 0)
+    inst = workload()
+    net = FlyChessNet(inst.conn, ModelConfig(steps=STEPS_T))
+    synth.apply(net.brain, inst)
+    w, b = synth.encoder_weights(len(inst.in_idx))
+    with torch.no_grad():
+        net.encoder.weight.copy_(torch.from_numpy(w))
+        net.encoder.bias.copy_(torch.from_numpy(b))
+        params = dict(net.named_parameters())
+        for k, v in synth.head_weights(len(inst.out_idx)).items():
+            params[k].copy_(torch.from_numpy(v))
+    net = net.to(dev).eval()
+    rng = np.random.default_rng(5)
+    B = args.batch
+    rounds = []
+    for k in range(4):
+        x = synth.boards(B, 100 + k).astype(np.float16)
+        rows = np.repeat(np.arange(B), 30)
+        cols = np.concatenate([rng.choice(4168, 30, replace=False) for _ in range(B)])
+        rounds.append((x, rows, cols))
+
+    class Eager:                                  # chessfly/model.py:120-132, eager
+        @torch.no_grad()
+        def submit(self, x, rows, cols):
+            logits, wdl = net(torch.from_numpy(x).to(dev, non_blocking=True).float())
+            legal = logits[torch.from_numpy(rows).to(dev, non_blocking=True), torch.from_numpy(cols).to(dev, non_blocking=True)]
+            return legal.float(), net.expected_value(wdl.float())
+
+        @staticmethod
+        def result(h):
+            return h[0].cpu().numpy(), h[1].float().cpu().numpy()
+
+    out = {}
+    for name, ev in (("reference_eager", Eager()), ("evaluator", Evaluator(net, dev, graphs=False)),
+                     ("evaluator_graphs", Evaluator(net, dev, graphs=True))):
+        def play(n):
+            inflight = None
+            for k in range(n):
+                h = ev.submit(*rounds[k % len(rounds)])
+                if inflight is not None:
+                    ev.result(inflight)
+                inflight = h
+            ev.result(inflight)
+        play(args.warmup + 1)
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        play(args.steps)
+        torch.cuda.synchronize(dev)
+        el = time.perf_counter() - t0
+        out[name] = {"positions_per_s": round(B * args.steps / el, 1), "ms_per_round": round(1000 * el / args.steps, 3)}
+    print(json.dumps({"metric": "self-play evaluator positions/sec (FlyChessNet rounds, legal-move logits + values)",
+                      "unit": UNIT, "positions_per_round": B, "legal_moves_per_position": 30, "rounds": args.steps,
+                      "warmup": args.warmup, "timing": "host wall clock around whole rounds (submit .. result), "
+                      "one round in flight", "results": out}), flush=True)
+
+
 def main():
     args = parse()
     rank, world, local = init_dist(args)
@@ -345,6 +413,8 @@ def main():
         return probe_arm(args)
     if args.train:
         return train_arm(args, rank, world, local)
+    if args.evaluator:
+        return evaluator_arm(args)
     from alphafly_b200 import synth
     from alphafly_b200.brain import ConnectomeRNN
     dev = torch.device("cuda", local)

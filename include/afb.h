@@ -177,6 +177,20 @@ AFB_API int afb_graph_forward(const afb_graph *graph, const float *w, const floa
                       float h_max, const float *u, int64_t ld_u, int64_t batch, int steps, float *h,
                       int64_t ld_h, void *workspace, size_t workspace_bytes, void *stream);
 
+/* ---- policy head: legal-move logits only (chessfly/model.py:104 + 124-126) --------------------------
+ * The reference evaluates the dense policy logits (B, N_MOVES) = r W^T + b + F[:, move_from] + T[:, move_to]
+ * and then gathers logits[rows, cols] of the legal moves.  This entry point computes only the m gathered
+ * entries:  out[i] = r[rows[i]] . w[cols[i]] + b[cols[i]] + f[rows[i], move_from[cols[i]]]
+ *                                                         + t[rows[i], move_to[cols[i]]]
+ * r (batch, n_out) and w (n_moves, n_out) row-major float32; b (n_moves); f, t (batch, n_sq) row-major
+ * (the factorised from/to terms, already multiplied out); move_from, move_to (n_moves) int64 in [0, n_sq).
+ * rows in [0, batch) and cols in [0, n_moves) as int64; an index out of range gives NaN for that entry.
+ * One warp per entry; asynchronous on `stream`. */
+AFB_API int afb_legal_logits(int64_t m, const int64_t *rows, const int64_t *cols, int64_t batch, int64_t n_out,
+                             const float *r, int64_t n_moves, const float *w, const float *b, int64_t n_sq,
+                             const float *f, const float *t, const int64_t *move_from, const int64_t *move_to,
+                             float *out, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

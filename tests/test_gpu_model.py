@@ -78,3 +78,115 @@ def test_train_step_matches_reference():
         assert np.mean(np.abs(step - step_ref) <= 1e-6 + 1e-3 * np.abs(step_ref)) > 0.999, k
     np.testing.assert_allclose(net.norm.mean.cpu().numpy(), g["norm_mean"], rtol=1e-5, atol=1e-6)
     np.testing.assert_allclose(net.norm.var.cpu().numpy(), g["norm_var"], rtol=1e-4, atol=1e-7)
+
+
+def _plain(net, x, rows, cols):
+    """The reference's Evaluator.submit + result (chessfly/model.py:120-132), eager."""
+    net.eval()
+    with torch.no_grad():
+        logits, wdl = net(torch.from_numpy(x).to(DEV).float())
+        v = net.expected_value(wdl.float()).cpu().numpy()
+        if rows is None:
+            return logits.half().cpu().numpy(), v
+        return logits[torch.from_numpy(rows).to(DEV), torch.from_numpy(cols).to(DEV)].float().cpu().numpy(), v
+
+
+@pytest.fixture(scope="module")
+def small_net():
+    inst = synth.small()
+    net = FlyChessNet(inst.conn, ModelConfig(steps=6))
+    synth.apply(net.brain, inst)
+    w, b = synth.encoder_weights(len(inst.in_idx))
+    with torch.no_grad():
+        net.encoder.weight.copy_(torch.from_numpy(w))
+        net.encoder.bias.copy_(torch.from_numpy(b))
+        params = dict(net.named_parameters())
+        for k, v in synth.head_weights(len(inst.out_idx)).items():
+            params[k].copy_(torch.from_numpy(v))
+        params["policy_from.weight"].normal_(0, 0.05, generator=torch.Generator().manual_seed(3))
+        params["policy_to.weight"].normal_(0, 0.05, generator=torch.Generator().manual_seed(4))
+    return net.to(DEV)
+
+
+def _request(batch, seed):
+    rng = np.random.default_rng(seed)
+    x = synth.boards(batch, seed).astype(np.float16)
+    rows = np.repeat(np.arange(batch), 30)
+    cols = np.concatenate([rng.choice(4168, 30, replace=False) for _ in range(batch)])
+    return x, rows, cols
+
+
+@pytest.mark.parametrize("graphs", [False, True])
+@pytest.mark.parametrize("batch", [7, 300])
+def test_pipelined_evaluator_equals_the_reference_evaluation(small_net, graphs, batch):
+    """Pinned staging, CUDA-graph replay (bucket of 256 or 512 positions) and the fused legal-logit kernel
+    give the reference Evaluator's results: same values, legal logits to float32 rounding."""
+    ev = Evaluator(small_net, DEV, graphs=graphs)
+    x, rows, cols = _request(batch, batch)
+    ref_legal, ref_values = _plain(small_net, x, rows, cols)
+    legal, values = ev(x, rows, cols)
+    assert legal.shape == ref_legal.shape and legal.dtype == np.float32
+    np.testing.assert_allclose(legal, ref_legal, rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(values, ref_values, rtol=1e-5, atol=1e-6)
+    lazy, lazy_values = ev(x, None, None)
+    ref_lazy, _ = _plain(small_net, x, None, None)
+    assert lazy.shape == (batch, 4168) and lazy.dtype == np.float16
+    np.testing.assert_allclose(lazy.astype(np.float32), ref_lazy.astype(np.float32), rtol=2e-3, atol=2e-3)
+
+
+def test_two_rounds_in_flight_and_weight_updates_between_rounds(small_net):
+    """The self-play loop's pipelining (submit round k+1 before fetching round k), and a parameter update
+    between rounds (as a training phase does) reaching the captured graph."""
+    ev = Evaluator(small_net, DEV, graphs=True)
+    a, b = _request(200, 1), _request(200, 2)
+    ha = ev.submit(*a)
+    hb = ev.submit(*b)
+    ra, rb = ev.result(ha), ev.result(hb)
+    np.testing.assert_allclose(ra[0], _plain(small_net, *a)[0], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(rb[0], _plain(small_net, *b)[0], rtol=1e-4, atol=1e-4)
+    hc = ev.submit(*a)                                   # reuses round a's pinned buffers
+    ev.submit(*b)
+    ev.submit(*b)                                        # a third submit before any result: hc is kept
+    np.testing.assert_array_equal(ev.result(hc)[0], ra[0])
+    with torch.no_grad():
+        small_net.brain.bias.add_(0.3)                   # in place: bumps the version the graph checks
+        small_net.policy.bias.add_(1.0)
+    try:
+        moved = ev(*a)
+        ref = _plain(small_net, *a)
+        np.testing.assert_allclose(moved[0], ref[0], rtol=1e-4, atol=1e-4)
+        np.testing.assert_allclose(moved[1], ref[1], rtol=1e-5, atol=1e-6)
+        assert not np.allclose(moved[1], ra[1])
+    finally:
+        with torch.no_grad():
+            small_net.brain.bias.sub_(0.3)
+            small_net.policy.bias.sub_(1.0)
+
+
+def test_legal_logits_kernel_against_torch():
+    """afb_legal_logits at the real head sizes (2,333 outputs, 4,168 moves, 64 squares) against the dense
+    product and gather in float64; an out-of-range index gives NaN for its entry only."""
+    from alphafly_b200 import _lib
+    from alphafly_b200.encoding import move_squares
+    g = torch.Generator(device=DEV).manual_seed(0)
+    batch, o = 64, 2333
+    r = torch.randn(batch, o, device=DEV, generator=g)
+    w = torch.randn(4168, o, device=DEV, generator=g) / o ** 0.5
+    b = torch.randn(4168, device=DEV, generator=g)
+    f = torch.randn(batch, 64, device=DEV, generator=g)
+    t = torch.randn(batch, 64, device=DEV, generator=g)
+    frm, to = (torch.as_tensor(a, device=DEV) for a in move_squares())
+    rows = torch.randint(0, batch, (5000,), device=DEV, generator=g)
+    cols = torch.randint(0, 4168, (5000,), device=DEV, generator=g)
+    rows[17], cols[18] = batch, -1                       # out of range
+    out = torch.empty(5000, device=DEV)
+    lib = _lib.load()
+    _lib.check(lib.afb_legal_logits(5000, rows.data_ptr(), cols.data_ptr(), batch, o, r.data_ptr(), 4168, w.data_ptr(),
+                                    b.data_ptr(), 64, f.data_ptr(), t.data_ptr(), frm.data_ptr(), to.data_ptr(),
+                                    out.data_ptr(), torch.cuda.current_stream().cuda_stream))
+    dense = (r.double() @ w.double().T + b.double() + f.double()[:, frm] + t.double()[:, to])
+    ok = torch.ones(5000, dtype=torch.bool, device=DEV)
+    ok[17] = ok[18] = False
+    ref = dense[rows[ok], cols[ok]]
+    assert torch.isnan(out[17]) and torch.isnan(out[18])
+    assert float((out[ok].double() - ref).abs().max()) < 1e-4
