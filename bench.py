@@ -490,6 +490,18 @@ def main():
                      "l2_gather_ceiling_source": "afb_probe_gather: 2^25 uniform random rows of a "
                                                  f"{max(cone.rows_len):,} x 512 B slab, measured in this run"})
 
+    # the weight-version precompute (brain.py:238-252, 296-306): edge weights, resting trajectory, sub-matrix
+    # values and row constants, as after every training phase; events on the launching stream
+    with torch.no_grad():
+        w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for k in range(3):
+            if k == 2:
+                w0.record(stream)
+            cone.set_weight_tensors(1, rnn.edge_weights(), rnn.bias, rnn.alpha_logit, rnn.h_max)
+        w1.record(stream)
+        torch.cuda.synchronize(dev)
+        weight_version_ms = w0.elapsed_time(w1)
+
     e2e = None
     if not args.no_e2e:
         # Through the public call with host buffers: each step copies its drive from pinned host memory and
@@ -558,6 +570,7 @@ def main():
                            "parallelism": f"positions sharded over {world} GPU(s), wiring replicated, no collective"},
                 "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
                 "gpu_launches": args.steps * (STEPS_T + 1),
+                "weight_version_ms": round(weight_version_ms, 3),
                 "light_cone": {"rows": cone.rows_len, "nnz": cone.nnz, "edge_visits": cone.edge_visits}}
         print(json.dumps(line), flush=True)
     if world > 1:

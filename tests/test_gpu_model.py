@@ -190,3 +190,30 @@ def test_legal_logits_kernel_against_torch():
     ref = dense[rows[ok], cols[ok]]
     assert torch.isnan(out[17]) and torch.isnan(out[18])
     assert float((out[ok].double() - ref).abs().max()) < 1e-4
+
+
+def test_web_model_round_trip_evaluates_like_the_exported_network(small_net, tmp_path):
+    """export_web_model -> net_from_web_model on configuration 1's network: the manifest's test vectors
+    (float32 logits of legal moves and values, made on the original network) are reproduced by the rebuilt
+    network within the float16 rounding of the exported synapse, encoder and policy weights."""
+    from alphafly_b200 import webmodel
+    net = small_net
+    x, rows, cols = _request(10, 12)
+    legal = [cols[rows == k] for k in range(10)]
+    with torch.no_grad():
+        net.norm.mean.normal_(0, 0.1, generator=torch.Generator(device=DEV).manual_seed(1))
+    try:
+        tests = webmodel.make_test_vectors(net, x.astype(np.float32), legal)
+        webmodel.export_web_model(net, tmp_path, tests=tests)
+        back = webmodel.net_from_web_model(tmp_path, device=DEV)
+        again = webmodel.make_test_vectors(back, x.astype(np.float32), legal)
+        for a, b in zip(tests, again):
+            assert a["idx"] == b["idx"] and a["features"] == b["features"]
+            np.testing.assert_allclose(b["logits"], a["logits"], rtol=0, atol=2e-2)
+            assert abs(a["value"] - b["value"]) < 2e-2
+        ref = np.concatenate([t["logits"] for t in tests])
+        got = np.concatenate([t["logits"] for t in again])
+        assert orc.rel_l2(got, ref) < 5e-3
+    finally:
+        with torch.no_grad():
+            net.norm.mean.zero_()
