@@ -310,6 +310,8 @@ int afb_cone_forward_train(const afb_cone *c, const float *u_in, int64_t ld_u, i
             a.item_order = sp.op.item_order.get();
             a.bounds = sp.op.bounds.get();
             a.n_items = sp.op.n_items;
+            a.n_rows = sp.op.n_rows;
+            a.nnz = sp.op.nnz;
             a.rc = sp.rc[AFB_MODE_F32].get();
             a.x_in = x_in;
             a.ts_in = ts_in;

@@ -258,6 +258,8 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
             a.item_order = sp.op.item_order.get();
             a.bounds = sp.op.bounds.get();
             a.n_items = sp.op.n_items;
+            a.n_rows = sp.op.n_rows;
+            a.nnz = sp.op.nnz;
             a.rc = sp.rc[mode].get();
             a.x_in = x_in ? x_in : buf[(t + 1) & 1];   // step 1 reads no state (R_0 is empty)
             a.ts_in = ts_in;
@@ -329,6 +331,8 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
             a.item_order = m.item_order.get();
             a.bounds = m.bounds.get();
             a.n_items = m.n_items;
+            a.n_rows = m.n_rows;
+            a.nnz = m.nnz;
             a.rc = t == 1 ? rc_first : rc_rest;
             a.x_in = x_in;
             a.ts_in = ts;

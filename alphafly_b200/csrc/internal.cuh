@@ -71,6 +71,8 @@ struct StepArgs {
     const int *item_order;
     const int2 *bounds;
     int n_items;
+    int n_rows;                    // rows of this step's sub-matrix
+    int64_t nnz;                   // its synapses (chooses the kernel: see launch in step.cu)
     const RowConst *rc;
     const void *x_in;              // state of R_{t-1}, tile-major (see tile_cols)
     int64_t ts_in;                 // elements between consecutive batch tiles of x_in

@@ -761,6 +761,11 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
     }
 }
 
+#ifndef AFB_RING_MAX_DEGREE
+#define AFB_RING_MAX_DEGREE 16
+#endif
+constexpr int64_t kRingMaxDegree = AFB_RING_MAX_DEGREE;  // sub-matrices with shorter mean rows take the ring kernel
+
 template <typename T, typename TV>
 void launch(const StepArgs &a, cudaStream_t s) {
     constexpr int BT = 32 * Lane<T>::V;
@@ -768,7 +773,11 @@ void launch(const StepArgs &a, cudaStream_t s) {
     const int64_t tiles = (a.batch + BT - 1) / BT;
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
-    if (AFB_RING) {
+    // The ring kernel keeps gathers in flight across row ends, which pays on sub-matrices whose rows are
+    // shorter than half a 32-synapse window (measured on configuration 3: step 1, which has no synapses,
+    // 0.85 vs 1.04 ms); the register kernel wins on the others.  Both give bitwise the same results.
+    const bool ring = AFB_RING || a.nnz < kRingMaxDegree * (int64_t)a.n_rows;
+    if (ring) {
         static unsigned long long configured = 0;   // devices on which this instantiation may use kRingBytes
         int dev = 0;
         AFB_CUDA(cudaGetDevice(&dev));
