@@ -478,7 +478,7 @@ def main():
                 "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                 "traffic": measured_traffic() if B == 35_840 else None,
                 "traffic_source": "profiles/step_kernel_traffic_config3.txt (ncu, B = 35,840)",
-                "kernel": "step_kernel<__half,__half> (6 launches per forward)",
+                "kernel": "step_kernel<__half,__half> (steps 2-6) and step_kernel_ring (step 1): 6 launches per forward",
                 "algorithmic_bytes_per_launch": int(sum(per_step_bytes) / STEPS_T),
                 "launch_ms": [round(x, 3) for x in kernel_ms],
                 "l2_gather_bytes_per_forward": int(gathered),
