@@ -92,18 +92,42 @@ class FlyChessNet(nn.Module):
 
     def drive(self, x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
         """u_in (sensory neurons, batch) = input_gain * (W x^T + b), over the first N_BASE features unless
-        the attack planes are switched on (chessfly/model.py:98-102)."""
+        the attack planes are switched on (chessfly/model.py:98-102).  For the float16 inference path the
+        product runs on the tensor cores: float16 weights (a copy refreshed when the encoder changes) times
+        the float16 features (board bits, exact), accumulated in float32 and rounded once to the float16
+        drive the deviation path reads; everything else is float32 as in the reference."""
         k = N_FEATURES if self.cfg.attack_planes else N_BASE
         g = self.cfg.input_gain
+        if dtype == torch.float16 and x.is_cuda and not torch.is_grad_enabled():
+            w16, b16 = self.half_encoder()
+            return torch.addmm(b16.unsqueeze(1), w16, x[:, :k].half().T, beta=g, alpha=g)
         w, b = self.encoder.weight[:, :k], self.encoder.bias
-        u = torch.addmm(b.unsqueeze(1), w, x[:, :k].T, beta=g, alpha=g)
+        u = torch.addmm(b.unsqueeze(1), w, x[:, :k].float().T, beta=g, alpha=g)
         return u.to(dtype).contiguous()
+
+    @torch.no_grad()
+    def half_encoder(self) -> tuple[torch.Tensor, torch.Tensor]:
+        """The float16 copy of the encoder's weight (first k columns) and bias, rewritten in place when a
+        parameter changed (so a captured CUDA graph reading it stays valid)."""
+        k = N_FEATURES if self.cfg.attack_planes else N_BASE
+        w, b = self.encoder.weight, self.encoder.bias
+        key = (w._version, b._version)
+        where = (w.data_ptr(), b.data_ptr(), k)
+        c = getattr(self, "_enc16", None)
+        if c is None or c[1] != where:
+            c = [key, where, w[:, :k].half().contiguous(), b.half()]
+            self._enc16 = c
+        elif c[0] != key:
+            c[2].copy_(w[:, :k])
+            c[3].copy_(b)
+            c[0] = key
+        return c[2], c[3]
 
     def readout(self, x: torch.Tensor) -> torch.Tensor:
         """x: (B, N_FEATURES) -> the normalised output-neuron state r (B, len(out_idx)) the heads read
         (chessfly/model.py:97-103)."""
         dtype = self.infer_dtype if x.is_cuda and not torch.is_grad_enabled() else torch.float32
-        u_in = self.drive(x.float(), dtype)
+        u_in = self.drive(x, dtype)
         return self.norm(self.brain.forward_io(u_in, self.in_idx, self.out_idx, self.cfg.steps).T.float())
 
     def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
@@ -189,6 +213,8 @@ class Evaluator:
     def _refresh_constants(self) -> None:
         net, brain = self.net, self.net.brain
         mode = _lib.MODE_DEV16 if net.infer_dtype == torch.float16 else _lib.MODE_F32
+        if mode == _lib.MODE_DEV16:
+            net.half_encoder()
         cone = brain.light_cone(net.in_idx, net.out_idx, net.cfg.steps)
         cone.set_weights(brain, mode, brain._weight_key(mode, cone))
 
