@@ -330,22 +330,7 @@ struct Gather<float> {
     }
 };
 
-// finish_row with the row's constants already at hand (shared memory)
-template <typename T>
-__device__ __forceinline__ void load_stream(const T *p, float (&x)[Lane<T>::V], uint64_t pol) {
-    const uint4 v = ld_stream_v4(p, pol);
-    if constexpr (sizeof(T) == 4) {
-        x[0] = __uint_as_float(v.x); x[1] = __uint_as_float(v.y); x[2] = __uint_as_float(v.z); x[3] = __uint_as_float(v.w);
-    } else {
-        const __half2 *h = reinterpret_cast<const __half2 *>(&v);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 f = __half22float2(h[k]);
-            x[2 * k] = f.x;
-            x[2 * k + 1] = f.y;
-        }
-    }
-}
+// V state values of this lane stored as one 16-byte word with an L2 eviction policy
 template <typename T>
 __device__ __forceinline__ void store_stream(T *p, const float (&x)[Lane<T>::V], uint64_t pol) {
     uint4 v;
@@ -619,9 +604,6 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_RING_MINBLOCKS) step_kernel_r
 #ifndef AFB_FULL_WINDOW
 #define AFB_FULL_WINDOW 1    // unpredicated path for the full chunks of a window
 #endif
-#ifndef AFB_GATHER_HINT
-#define AFB_GATHER_HINT 0    // 1: L2 evict-last on the gathered rows, evict-first on the indices and values
-#endif
 constexpr int kChunkR = AFB_CHUNK;
 
 // Per-warp loop bounds live in shared memory and are re-read where they are needed (volatile), so
@@ -693,39 +675,27 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
             int my_col = 0;
             uint32_t my_val = 0u;
             if (lane < n) {
-                if (AFB_GATHER_HINT) {
-                    const uint64_t once = policy_stream();
-                    my_col = (int)ld_stream_b32(a.col + eoff, once);
-                    my_val = G::bits(static_cast<const TV *>(a.val) + eoff, once);
-                } else {
-                    my_col = ld_once(a.col + eoff);
-                    my_val = G::bits_plain(static_cast<const TV *>(a.val) + eoff);
-                }
+                my_col = ld_once(a.col + eoff);
+                my_val = G::bits_plain(static_cast<const TV *>(a.val) + eoff);
             }
             // full chunks: nothing predicated (chunks kept in sequence: one chunk's rows in registers at a time)
             const int n_full = AFB_FULL_WINDOW ? n / kChunkR * kChunkR : 0;
 #pragma unroll 1
             for (int k = 0; k < n_full; k += kChunkR) {
                 uint4 x[kChunkR];
-                const uint64_t keep = AFB_GATHER_HINT ? policy_keep() : 0;
 #pragma unroll
-                for (int u = 0; u < kChunkR; ++u) {
-                    const T *src = x_tile + __shfl_sync(kFull, my_col, k + u) * BT;
-                    x[u] = AFB_GATHER_HINT ? ld_stream_v4(src, keep) : __ldg(reinterpret_cast<const uint4 *>(src));
-                }
+                for (int u = 0; u < kChunkR; ++u)
+                    x[u] = __ldg(reinterpret_cast<const uint4 *>(x_tile + __shfl_sync(kFull, my_col, k + u) * BT));
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) G::fma(acc, __shfl_sync(kFull, my_val, k + u), x[u]);
             }
             // the window's last, partial chunk
             for (int k = n_full; k < n; k += kChunkR) {
                 uint4 x[kChunkR];
-                const uint64_t keep = AFB_GATHER_HINT ? policy_keep() : 0;   // re-created per chunk: no live register
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) {
                     const int c = __shfl_sync(kFull, my_col, (k + u) & 31);
-                    const T *src = x_tile + c * BT;
-                    x[u] = k + u >= n ? make_uint4(0, 0, 0, 0)
-                                      : AFB_GATHER_HINT ? ld_stream_v4(src, keep) : __ldg(reinterpret_cast<const uint4 *>(src));
+                    x[u] = k + u >= n ? make_uint4(0, 0, 0, 0) : __ldg(reinterpret_cast<const uint4 *>(x_tile + c * BT));
                 }
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) G::fma(acc, __shfl_sync(kFull, my_val, (k + u) & 31), x[u]);
