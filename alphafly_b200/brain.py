@@ -359,6 +359,16 @@ class ConnectomeRNN(nn.Module):
     def csr_t(self, w: torch.Tensor) -> torch.Tensor:
         return torch.sparse_csr_tensor(self.t_crow, self.t_col, w[self.t_order], (self.n, self.n), check_invariants=False)
 
+    def __deepcopy__(self, memo):
+        """A copy without the native handles (light cone, whole-graph CSR): the copy builds its own on first
+        use, on whatever device it is moved to."""
+        import copy
+        new = self.__class__.__new__(self.__class__)
+        memo[id(self)] = new
+        for k, v in self.__dict__.items():
+            new.__dict__[k] = None if k in ("_cone", "_graph_cache", "_all_idx") else copy.deepcopy(v, memo)
+        return new
+
     # -- the literal recurrence ---------------------------------------------------------------------
     def _graph(self) -> _Graph:
         key = (self.pre.data_ptr(), str(self.pre.device))

@@ -243,6 +243,12 @@ class Evaluator:
     @torch.no_grad()
     def submit(self, x, rows, cols):
         """Launch the evaluation and return at once; ``result`` waits for it."""
+        if self.device.type != "cuda":
+            return self._submit(x, rows, cols)
+        with torch.cuda.device(self.device):       # the library, the graphs and the events use the current device
+            return self._submit(x, rows, cols)
+
+    def _submit(self, x, rows, cols):
         net = self.net
         net.eval()
         slot = self._turn
@@ -303,6 +309,80 @@ class _Done:
     @staticmethod
     def synchronize():
         pass
+
+
+class _ShardedHandle:
+    def __init__(self, parts, n_legal, lazy):
+        self.parts, self.n_legal, self.lazy = parts, n_legal, lazy    # [(handle, lo, hi, legal positions)]
+        self.value = None
+
+    def get(self):
+        if self.value is None:
+            vals = [h.get() for h, _, _, _ in self.parts]
+            values = np.concatenate([v for _, v in vals]) if vals else np.zeros(0, np.float32)
+            if self.lazy:
+                out = np.concatenate([o for o, _ in vals]) if vals else np.zeros((0, N_MOVES), np.float16)
+            else:
+                out = np.empty(self.n_legal, np.float32)
+                for (o, _), (_, _, _, sel) in zip(vals, self.parts):
+                    out[sel] = o
+            self.value = (out, values)
+        return self.value
+
+
+class ShardedEvaluator:
+    """The Evaluator contract over several GPUs of one process (the MCTS leaf batch of chessfly/mcts.py:
+    263-301 spread across devices): a round's positions are split into contiguous shares, one per device,
+    each evaluated by an ``Evaluator`` on that device's replica of the network, concurrently (every
+    share's work is queued before any result is waited for); legal-move logits come back in the order
+    of the request's (rows, cols), values in position order.
+
+    The replicas copy the primary network at construction; after a training phase changes it, ``sync``
+    copies its parameters and buffers into them in place (so their captured graphs stay valid)."""
+
+    def __init__(self, net: FlyChessNet, devices, graphs: bool = True, max_graphs: int = 4):
+        import copy
+        self.net = net
+        self.devices = [torch.device(d) for d in devices]
+        self.replicas = []
+        for d in self.devices:
+            r = copy.deepcopy(net).to(d)
+            r.infer_dtype = net.infer_dtype
+            self.replicas.append(r)
+        self.evaluators = [Evaluator(r, d, graphs=graphs, max_graphs=max_graphs) for r, d in zip(self.replicas, self.devices)]
+
+    @torch.no_grad()
+    def sync(self) -> None:
+        src = dict(self.net.state_dict(keep_vars=True))
+        for r in self.replicas:
+            for k, t in r.state_dict(keep_vars=True).items():
+                s = src[k]
+                if not torch.equal(t.detach(), s.detach().to(t.device)):
+                    t.detach().copy_(s.detach())
+            r.infer_dtype = self.net.infer_dtype
+
+    def submit(self, x, rows, cols):
+        b = len(x)
+        g = len(self.evaluators)
+        bounds = [b * k // g for k in range(g + 1)]
+        rows_np = None if rows is None else np.asarray(rows, np.int64)
+        cols_np = None if cols is None else np.asarray(cols, np.int64)
+        parts = []
+        for ev, lo, hi in zip(self.evaluators, bounds[:-1], bounds[1:]):
+            if hi == lo:
+                continue
+            if rows_np is None:
+                parts.append((ev.submit(x[lo:hi], None, None), lo, hi, None))
+            else:
+                sel = np.flatnonzero((rows_np >= lo) & (rows_np < hi))
+                parts.append((ev.submit(x[lo:hi], rows_np[sel] - lo, cols_np[sel]), lo, hi, sel))
+        return _ShardedHandle(parts, 0 if rows_np is None else len(rows_np), rows is None)
+
+    def result(self, handle):
+        return handle.get()
+
+    def __call__(self, x, rows, cols):
+        return self.result(self.submit(x, rows, cols))
 
 
 NEW_HEADS = ("policy_from.", "policy_to.")

@@ -381,8 +381,12 @@ def evaluator_arm(args):
             return h[0].cpu().numpy(), h[1].float().cpu().numpy()
 
     out = {}
-    for name, ev in (("reference_eager", Eager()), ("evaluator", Evaluator(net, dev, graphs=False)),
-                     ("evaluator_graphs", Evaluator(net, dev, graphs=True))):
+    arms = [("reference_eager", Eager()), ("evaluator", Evaluator(net, dev, graphs=False)),
+            ("evaluator_graphs", Evaluator(net, dev, graphs=True))]
+    if args.gpus > 1:                             # one process, the round split over the visible GPUs
+        from alphafly_b200.model import ShardedEvaluator
+        arms.append((f"sharded_{args.gpus}_gpus", ShardedEvaluator(net, [f"cuda:{k}" for k in range(args.gpus)])))
+    for name, ev in arms:
         def play(n):
             inflight = None
             for k in range(n):

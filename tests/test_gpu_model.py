@@ -217,3 +217,32 @@ def test_web_model_round_trip_evaluates_like_the_exported_network(small_net, tmp
     finally:
         with torch.no_grad():
             net.norm.mean.zero_()
+
+
+@pytest.mark.parametrize("lazy", [False, True])
+def test_sharded_evaluator_equals_one_evaluator(small_net, lazy):
+    """ShardedEvaluator (two replicas; on a one-GPU box both live on cuda:0, which exercises the split and
+    the reassembly) returns what one Evaluator returns, for a request whose (rows, cols) are not grouped
+    by position; after a parameter change, sync() brings the replicas along."""
+    from alphafly_b200.model import ShardedEvaluator
+    devices = [f"cuda:{k % torch.cuda.device_count()}" for k in range(2)]
+    x, rows, cols = _request(301, 21)
+    perm = np.random.default_rng(0).permutation(len(rows))
+    rows, cols = rows[perm], cols[perm]
+    one = Evaluator(small_net, DEV)
+    many = ShardedEvaluator(small_net, devices)
+    req = (x, None, None) if lazy else (x, rows, cols)
+    a, b = one(*req), many(*req)
+    assert a[0].shape == b[0].shape and a[0].dtype == b[0].dtype
+    np.testing.assert_allclose(b[0].astype(np.float32), a[0].astype(np.float32), rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(b[1], a[1], rtol=1e-6, atol=1e-7)
+    with torch.no_grad():
+        small_net.brain.bias.add_(0.2)
+    try:
+        many.sync()
+        c, d = one(*req), many(*req)
+        np.testing.assert_allclose(d[1], c[1], rtol=1e-6, atol=1e-7)
+        assert not np.allclose(c[1], a[1])
+    finally:
+        with torch.no_grad():
+            small_net.brain.bias.sub_(0.2)

@@ -38,3 +38,15 @@ def test_load_weights_accepts_old_checkpoints_and_rejects_incomplete_ones():
     assert float(net.encoder.weight[:, N_BASE:].abs().sum()) == 0
     with pytest.raises(RuntimeError, match="does not match"):
         load_weights(net, {k: v for k, v in old.items() if k != "value.bias"})
+
+
+def test_deepcopy_drops_native_handles_and_copies_parameters():
+    """ShardedEvaluator replicates the network with copy.deepcopy: the cached light cone (a native handle)
+    is not copied, parameters and buffers are (new storage, same values)."""
+    import copy
+    net = FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3))
+    net.brain._cone = ("key", object())
+    c = copy.deepcopy(net)
+    assert c.brain._cone is None and net.brain._cone is not None
+    for (k, a), (_, b) in zip(net.state_dict().items(), c.state_dict().items()):
+        assert torch.equal(a, b) and (a.numel() == 0 or a.data_ptr() != b.data_ptr()), k
