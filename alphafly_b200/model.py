@@ -234,7 +234,9 @@ class Evaluator:
                 self._trunk(x)
         torch.cuda.current_stream(self.device).wait_stream(side)
         g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+        # capture on a stream of this device (torch's default capture stream belongs to the device that
+        # was current when it was first made)
+        with torch.cuda.graph(g, stream=torch.cuda.Stream(self.device)):
             outs = self._trunk(x)
         entry = (g, x, outs)
         self._graphs[key] = entry
