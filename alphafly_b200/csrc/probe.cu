@@ -51,6 +51,41 @@ __global__ void __launch_bounds__(kProbeThreads) gather_probe_ldg(const uint4 *_
     if (lane == 0) sink[warp] = x;
 }
 
+// Register path with 8-byte lanes: rows of 256 bytes (slab_rows x 2 of them), lane l taking bytes
+// [8 l, 8 l + 8), kProbeUnroll loads in flight per lane.
+template <int kProbeUnroll>
+__global__ void __launch_bounds__(kProbeThreads) gather_probe_ldg_narrow(const uint2 *__restrict__ slab, int64_t slab_rows,
+                                                                         const int *__restrict__ rows, int64_t n_rows,
+                                                                         uint32_t *__restrict__ sink) {
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = ((int64_t)blockIdx.x * kProbeThreads + threadIdx.x) >> 5;
+    const int64_t n_warps = ((int64_t)gridDim.x * kProbeThreads) >> 5;
+    const int64_t half_rows = 2 * slab_rows;
+    uint32_t x = 0;
+    int64_t r = warp;
+    for (; r + (kProbeUnroll - 1) * n_warps < n_rows; r += kProbeUnroll * n_warps) {
+        int idx[kProbeUnroll];
+#pragma unroll
+        for (int u = 0; u < kProbeUnroll; ++u) idx[u] = __ldg(rows + r + u * n_warps);
+        uint2 v[kProbeUnroll];
+#pragma unroll
+        for (int u = 0; u < kProbeUnroll; ++u)
+            v[u] = (uint64_t)idx[u] < (uint64_t)half_rows ? __ldg(slab + (int64_t)idx[u] * 32 + lane) : make_uint2(0, 0);
+#pragma unroll
+        for (int u = 0; u < kProbeUnroll; ++u) x ^= v[u].x ^ v[u].y;
+    }
+    for (; r < n_rows; r += n_warps) {
+        const int i = __ldg(rows + r);
+        if ((uint64_t)i < (uint64_t)half_rows) {
+            const uint2 v = __ldg(slab + (int64_t)i * 32 + lane);
+            x ^= v.x ^ v.y;
+        }
+    }
+#pragma unroll
+    for (int s = 16; s > 0; s >>= 1) x ^= __shfl_xor_sync(kAll, x, s);
+    if (lane == 0) sink[warp] = x;
+}
+
 __device__ __forceinline__ uint4 lds16(uint32_t addr) {
     uint4 v;
     asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
@@ -226,8 +261,9 @@ int64_t afb_probe_gather_sink_words(void) {
 int afb_probe_gather(int path, int blocks_per_sm, const void *slab, int64_t slab_rows, const int32_t *rows, int64_t n_rows,
                      uint32_t *sink, int64_t sink_words, void *stream) {
     return guarded([&] {
-        AFB_CHECK(path >= AFB_PROBE_LDG && path <= AFB_PROBE_LDG16, "afb_probe_gather: unknown path");
-        const bool ldg = path == AFB_PROBE_LDG || path == AFB_PROBE_LDG4 || path == AFB_PROBE_LDG16;
+        AFB_CHECK(path >= AFB_PROBE_LDG && path <= AFB_PROBE_LDG_NARROW16, "afb_probe_gather: unknown path");
+        const bool ldg = path == AFB_PROBE_LDG || path == AFB_PROBE_LDG4 || path == AFB_PROBE_LDG16 ||
+                         path == AFB_PROBE_LDG_NARROW8 || path == AFB_PROBE_LDG_NARROW16;
         if (blocks_per_sm <= 0) blocks_per_sm = ldg ? kProbeBlocksPerSm : kRingBlocksPerSm;
         AFB_CHECK(blocks_per_sm <= (ldg ? kProbeBlocksPerSm : kRingBlocksPerSm), "afb_probe_gather: too many blocks per SM");
         AFB_CHECK(slab && rows && sink, "afb_probe_gather: null pointer");
@@ -249,6 +285,14 @@ int afb_probe_gather(int path, int blocks_per_sm, const void *slab, int64_t slab
             break;
         case AFB_PROBE_LDG16:
             gather_probe_ldg<16><<<grid, kProbeThreads, 0, s>>>(sl, slab_rows, rows, n_rows, sink);
+            break;
+        case AFB_PROBE_LDG_NARROW8:
+            gather_probe_ldg_narrow<8><<<grid, kProbeThreads, 0, s>>>(static_cast<const uint2 *>(slab), slab_rows, rows,
+                                                                      n_rows, sink);
+            break;
+        case AFB_PROBE_LDG_NARROW16:
+            gather_probe_ldg_narrow<16><<<grid, kProbeThreads, 0, s>>>(static_cast<const uint2 *>(slab), slab_rows, rows,
+                                                                       n_rows, sink);
             break;
         case AFB_PROBE_CPASYNC:
             allow_ring(gather_probe_cpasync<false>);

@@ -89,8 +89,9 @@ def gather_ceiling(dev, slab_rows, n_rows=1 << 25, reps=5, path=0, blocks_per_sm
     from alphafly_b200 import _lib
     lib = _lib.load()
     g = torch.Generator(device=dev).manual_seed(5)
+    narrow = path in (7, 8)                       # 256-byte rows: each slab row counts as two
     slab = torch.randint(0, 1 << 30, (slab_rows, 128), dtype=torch.int32, device=dev, generator=g)
-    rows = torch.randint(0, slab_rows, (n_rows,), dtype=torch.int32, device=dev, generator=g)
+    rows = torch.randint(0, slab_rows * (2 if narrow else 1), (n_rows,), dtype=torch.int32, device=dev, generator=g)
     words = lib.afb_probe_gather_sink_words()
     sink = torch.empty(words, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -104,7 +105,7 @@ def gather_ceiling(dev, slab_rows, n_rows=1 << 25, reps=5, path=0, blocks_per_sm
         b.synchronize()
         if k >= 3:
             times.append(a.elapsed_time(b))
-    return n_rows * 512 / (statistics.median(times) / 1000.0) / 1e9
+    return n_rows * (256 if narrow else 512) / (statistics.median(times) / 1000.0) / 1e9
 
 
 def workload(seed=0):
