@@ -310,6 +310,10 @@ int afb_cone_forward_train(const afb_cone *c, const float *u_in, int64_t ld_u, i
             a.item_order = sp.op.item_order.get();
             a.bounds = sp.op.bounds.get();
             a.n_items = sp.op.n_items;
+            a.item_rows_fine = sp.op.fine.item_rows.get();
+            a.item_order_fine = sp.op.fine.item_order.get();
+            a.bounds_fine = sp.op.fine.bounds.get();
+            a.n_items_fine = sp.op.fine.n_items;
             a.n_rows = sp.op.n_rows;
             a.nnz = sp.op.nnz;
             a.rc = sp.rc[AFB_MODE_F32].get();

@@ -180,29 +180,43 @@ int bits_for(long long v) {
 
 }  // namespace
 
-void build_schedule(Csr &m, cudaStream_t s) {
-    std::vector<int> crow = to_host(m.crow.get(), (size_t)m.n_rows + 1, s);
-    std::vector<int> starts{0};
+// Items of about `target` cost units (a unit is a synapse, a row is kRowCost), heaviest first.
+static void make_items(const std::vector<int> &crow, int n_rows, int64_t target, std::vector<int> &starts,
+                       std::vector<int> &order) {
     std::vector<int64_t> cost;
+    starts.assign(1, 0);
     int64_t acc = 0;
-    for (int r = 0; r < m.n_rows; ++r) {
+    for (int r = 0; r < n_rows; ++r) {
         acc += (int64_t)(crow[r + 1] - crow[r]) + kRowCost;
-        if (acc >= kItemCost || r + 1 == m.n_rows) {
+        if (acc >= target || r + 1 == n_rows) {
             starts.push_back(r + 1);
             cost.push_back(acc);
             acc = 0;
         }
     }
-    if (m.n_rows == 0) cost.clear(), starts.assign(1, 0);
-    m.n_items = (int)cost.size();
-    std::vector<int> order(m.n_items);
+    if (n_rows == 0) cost.clear(), starts.assign(1, 0);
+    order.resize(cost.size());
     std::iota(order.begin(), order.end(), 0);
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+}
+
+void build_schedule(Csr &m, cudaStream_t s) {
+    std::vector<int> crow = to_host(m.crow.get(), (size_t)m.n_rows + 1, s);
+    std::vector<int> starts, order;
+    make_items(crow, m.n_rows, kItemCost, starts, order);
+    m.n_items = (int)order.size();
     m.item_rows.alloc(starts.size());
     to_device(m.item_rows.get(), starts, s);
     m.item_order.alloc(order.size());
     to_device(m.item_order.get(), order, s);
-    build_bounds(m, s);
+    build_bounds(m, m.n_items, m.item_rows.get(), m.bounds, s);
+    make_items(crow, m.n_rows, kFineItemCost, starts, order);
+    m.fine.n_items = (int)order.size();
+    m.fine.item_rows.alloc(starts.size());
+    to_device(m.fine.item_rows.get(), starts, s);
+    m.fine.item_order.alloc(order.size());
+    to_device(m.fine.item_order.get(), order, s);
+    build_bounds(m, m.fine.n_items, m.fine.item_rows.get(), m.fine.bounds, s);
 }
 
 }  // namespace afb

@@ -258,6 +258,10 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
             a.item_order = sp.op.item_order.get();
             a.bounds = sp.op.bounds.get();
             a.n_items = sp.op.n_items;
+            a.item_rows_fine = sp.op.fine.item_rows.get();
+            a.item_order_fine = sp.op.fine.item_order.get();
+            a.bounds_fine = sp.op.fine.bounds.get();
+            a.n_items_fine = sp.op.fine.n_items;
             a.n_rows = sp.op.n_rows;
             a.nnz = sp.op.nnz;
             a.rc = sp.rc[mode].get();
@@ -331,6 +335,10 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
             a.item_order = m.item_order.get();
             a.bounds = m.bounds.get();
             a.n_items = m.n_items;
+            a.item_rows_fine = m.fine.item_rows.get();
+            a.item_order_fine = m.fine.item_order.get();
+            a.bounds_fine = m.fine.bounds.get();
+            a.n_items_fine = m.fine.n_items;
             a.n_rows = m.n_rows;
             a.nnz = m.nnz;
             a.rc = t == 1 ? rc_first : rc_rest;

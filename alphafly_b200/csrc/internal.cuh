@@ -18,7 +18,16 @@ struct __align__(16) RowConst {
 };
 static_assert(sizeof(RowConst) == 32, "RowConst is two 16-byte words");
 
-// A CSR matrix (int32 indices) with the work schedule of the fused step kernel.
+// A work schedule of the fused step kernel: contiguous row ranges ("items") of similar cost, launched
+// heaviest first, each with its merge-path cut over the CTA's warps.
+struct Schedule {
+    int n_items = 0;
+    DevBuf<int> item_rows;         // (n_items + 1) row boundaries
+    DevBuf<int> item_order;        // (n_items) launch order
+    DevBuf<int2> bounds;           // (n_items x (warps + 1)) merge-path cut of each item over the CTA's warps
+};
+
+// A CSR matrix (int32 indices) with the work schedules of the fused step kernel.
 struct Csr {
     int n_rows = 0, n_cols = 0;
     int64_t nnz = 0;
@@ -27,11 +36,13 @@ struct Csr {
     DevBuf<int> edges, post;       // edges (nnz): index into W's edge list; post (nnz): local row
     DevBuf<int> t_crow, t_col, t_order;  // CSR of the transpose, and the edge permutation into it
     DevBuf<int> t_heavy;           // (n_cols) rows of the transpose, longest first (backward launch order)
-    // schedule: contiguous row ranges ("items") of similar cost, launched heaviest first
+    // schedule of items of ~kItemCost, and of ~kFineItemCost for launches whose kItemCost items would be
+    // too few CTAs to fill the GPU (narrow batches on small graphs or small light-cone steps)
     int n_items = 0;
     DevBuf<int> item_rows;         // (n_items + 1) row boundaries
     DevBuf<int> item_order;        // (n_items) launch order
     DevBuf<int2> bounds;           // (n_items x (warps + 1)) merge-path cut of each item over the CTA's warps
+    Schedule fine;
 };
 
 struct Step {
@@ -57,10 +68,14 @@ struct Step {
 // Schedule target: cost units (edges + kRowCost per row) per CTA work item.
 constexpr int kRowCost = 4;
 constexpr int kItemCost = AFB_ITEM_COST;
+#ifndef AFB_FINE_ITEM_COST
+#define AFB_FINE_ITEM_COST 512
+#endif
+constexpr int kFineItemCost = AFB_FINE_ITEM_COST;
 
 // Builds the item schedule of `m` from its crow (device), then its merge-path table; synchronous.
 void build_schedule(Csr &m, cudaStream_t s);
-void build_bounds(Csr &m, cudaStream_t s);
+void build_bounds(const Csr &m, int n_items, const int *item_rows, DevBuf<int2> &bounds, cudaStream_t s);
 
 // Launch helpers of the fused step kernel (step.cu).
 struct StepArgs {
@@ -71,6 +86,10 @@ struct StepArgs {
     const int *item_order;
     const int2 *bounds;
     int n_items;
+    const int *item_rows_fine;     // the fine schedule (Csr::fine); the launcher picks one of the two
+    const int *item_order_fine;
+    const int2 *bounds_fine;
+    int n_items_fine;
     int n_rows;                    // rows of this step's sub-matrix
     int64_t nnz;                   // its synapses (chooses the kernel: see launch in step.cu)
     const RowConst *rc;

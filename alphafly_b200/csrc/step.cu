@@ -13,7 +13,8 @@
 // multiplication", SC'16): the merge of row ends with edge indices is cut into equal diagonals, so a
 // 5,000-synapse row and 60 short rows cost the same.  A row cut by warp boundaries leaves one partial
 // per warp in shared memory; after a barrier one warp sums them in warp order and finishes the row,
-// so results are bitwise reproducible and independent of the batch width.
+// so results are bitwise reproducible, and independent of the batch width among widths that select the same
+// item schedule (see launch: narrow launches take a finer one).
 //
 // The cost is the gather: every synapse pulls one 512-byte row of the previous state from L2.  Two
 // kernels implement it.  The default (step_kernel) loads kChunk gathered rows per lane straight into
@@ -736,11 +737,32 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
 #endif
 constexpr int64_t kRingMaxDegree = AFB_RING_MAX_DEGREE;  // sub-matrices with shorter mean rows take the ring kernel
 
+// CTAs below which a step takes the fine schedule: two waves of the register kernel's 5 CTAs per SM.
+int64_t fine_grid_limit() {
+    static int sms[64] = {0};
+    int dev = 0;
+    AFB_CUDA(cudaGetDevice(&dev));
+    if (dev >= 64) return 0;
+    if (!sms[dev]) AFB_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    return 2LL * AFB_MINBLOCKS * sms[dev];
+}
+
 template <typename T, typename TV>
-void launch(const StepArgs &a, cudaStream_t s) {
+void launch(const StepArgs &args, cudaStream_t s) {
     constexpr int BT = 32 * Lane<T>::V;
-    if (a.n_items == 0 || a.batch == 0) return;
-    const int64_t tiles = (a.batch + BT - 1) / BT;
+    if (args.n_items == 0 || args.batch == 0) return;
+    const int64_t tiles = (args.batch + BT - 1) / BT;
+    StepArgs a = args;
+    // Too few CTAs for two waves: the fine schedule (one batch tile of a small graph 2.8x faster).  The
+    // schedule fixes where rows are cut between warps, hence the summation order of those rows: results are
+    // bitwise the same for batch widths that pick the same schedules, and may differ in the last place of
+    // cut rows otherwise.
+    if (a.n_items_fine > a.n_items && tiles * a.n_items < fine_grid_limit()) {
+        a.n_items = a.n_items_fine;
+        a.item_rows = a.item_rows_fine;
+        a.item_order = a.item_order_fine;
+        a.bounds = a.bounds_fine;
+    }
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
     // The ring kernel keeps gathers in flight across row ends, which pays on sub-matrices whose rows are
@@ -787,12 +809,12 @@ __global__ void bounds_kernel(int n_items, int warps, const int *__restrict__ cr
 
 int tile_cols(int elem_bytes) { return 32 * (16 / elem_bytes); }
 
-void build_bounds(Csr &m, cudaStream_t s) {
+void build_bounds(const Csr &m, int n_items, const int *item_rows, DevBuf<int2> &bounds, cudaStream_t s) {
     const int warps = kWarps;
-    m.bounds.alloc((size_t)m.n_items * (warps + 1));
-    if (m.n_items) {
-        bounds_kernel<<<grid_for((int64_t)m.n_items * (warps + 1), 256), 256, 0, s>>>(m.n_items, warps, m.crow.get(),
-                                                                                       m.item_rows.get(), m.bounds.get());
+    bounds.alloc((size_t)n_items * (warps + 1));
+    if (n_items) {
+        bounds_kernel<<<grid_for((int64_t)n_items * (warps + 1), 256), 256, 0, s>>>(n_items, warps, m.crow.get(), item_rows,
+                                                                                     bounds.get());
         AFB_LAUNCHED();
     }
 }

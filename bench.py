@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--train", action="store_true",
                     help="time the training step instead (configuration 5: FlyChessNet train_step, B = 2,048 per GPU)")
     ap.add_argument("--probe", action="store_true", help="print the gather ceiling of every load path and exit")
+    ap.add_argument("--configs", action="store_true",
+                    help="time configurations 1, 2 and 4 (the other workloads of the scope; one JSON line each)")
     ap.add_argument("--evaluator", action="store_true",
                     help="time the self-play Evaluator (FlyChessNet rounds of --batch positions, 30 legal moves each)")
     args = ap.parse_args()
@@ -342,6 +344,62 @@ def train_arm(args, rank, world, local):
         torch.distributed.destroy_process_group()
 
 
+def configs_arm(args):
+    """The other configurations of the workload, one JSON line each, device time per forward (CUDA events,
+    median of ``--steps`` after ``--warmup``):
+      1  small synthetic graph (8,192 neurons, 400k synapses), float32 light-cone forward, B = 64;
+      2  full-scale graph, float32 literal recurrence over all 166,700 neurons (no pruning), B = 1,120;
+      4  shuffled control of configuration 1, float16 deviation, B = 1, 64, 1,120, 8,192, 65,536."""
+    from alphafly_b200 import synth
+    from alphafly_b200.brain import ConnectomeRNN
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        with torch.no_grad():
+            for _ in range(args.warmup):
+                fn()
+            times = []
+            for _ in range(args.steps):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record(stream)
+                fn()
+                b.record(stream)
+                b.synchronize()
+                times.append(a.elapsed_time(b))
+        return statistics.median(times)
+
+    def line(config, workload, batch, ms, dtype):
+        print(json.dumps({"metric": "connectome evals/sec (6-step fwd)", "config": config, "workload": workload,
+                          "batch": batch, "dtype": dtype, "ms_per_forward": round(ms, 4),
+                          "value": round(batch / (ms / 1000.0), 1), "unit": UNIT, "steps": args.steps,
+                          "warmup": args.warmup}), flush=True)
+
+    for name, inst in (("1", synth.small()), ("4", synth.shuffled())):
+        rnn = ConnectomeRNN(inst.conn)
+        synth.apply(rnn, inst)
+        rnn = rnn.to(dev)
+        in_idx, out_idx = inst.in_idx.to(dev), inst.out_idx.to(dev)
+        batches = (64,) if name == "1" else (1, 64, 1120, 8192, 65536)
+        for batch in batches:
+            u = torch.from_numpy(synth.drive(inst, min(batch, 2048), seed=7)).repeat(1, (batch + 2047) // 2048)[:, :batch]
+            u = u.contiguous().to(dev)
+            if name == "4":
+                u = u.half()
+            ms = timed(lambda: rnn.forward_io(u, in_idx, out_idx, STEPS_T))
+            line(name, "small synthetic, float32 light cone" if name == "1" else "shuffled control, float16 deviation",
+                 batch, ms, "f32" if name == "1" else "f16")
+        del rnn
+    inst = workload()
+    rnn = ConnectomeRNN(inst.conn)
+    synth.apply(rnn, inst)
+    rnn = rnn.to(dev)
+    u4 = torch.from_numpy(synth.drive(inst, 1120, seed=3))
+    full_u = torch.zeros(inst.n, 1120).index_copy_(0, inst.in_idx, u4).to(dev)
+    ms = timed(lambda: rnn(full_u, STEPS_T))
+    line("2", "full-scale graph, float32 literal recurrence (all neurons, no pruning)", 1120, ms, "f32")
+
+
 def evaluator_arm(args):
     """Self-play evaluation rounds (chessfly/workers.py:118-167): B positions per round with 30 legal moves
     each, one round in flight while the next is submitted.  Three implementations of the same contract:
@@ -420,6 +478,8 @@ def main():
         return train_arm(args, rank, world, local)
     if args.evaluator:
         return evaluator_arm(args)
+    if args.configs:
+        return configs_arm(args)
     from alphafly_b200 import synth
     from alphafly_b200.brain import ConnectomeRNN
     dev = torch.device("cuda", local)
