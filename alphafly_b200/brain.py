@@ -381,7 +381,11 @@ class ConnectomeRNN(nn.Module):
         Computed in float32 (float16 input gives a float16 result).  Unlike the reference's no-grad branch
         (chessfly/brain.py:218), ``u`` is not modified."""
         assert u.is_contiguous()
+        if u.dim() != 2 or u.shape[0] != self.n:
+            raise ValueError(f"u must be (N, B) = ({self.n}, B), got {tuple(u.shape)}")
         _require_cuda(u, "u")
+        if u.device != self.pre.device:
+            raise RuntimeError(f"u must be on the module's device {self.pre.device}")
         if u.dtype not in (torch.float32, torch.float16):
             raise TypeError(f"alphafly_b200 computes in float32 or float16, got {u.dtype}")
         if torch.is_grad_enabled() and (u.requires_grad or any(p.requires_grad for p in self.parameters())):
@@ -422,7 +426,11 @@ class ConnectomeRNN(nn.Module):
         """u_in: (len(in_idx), B) drive of the input neurons.  Returns the output neurons after ``steps``
         updates, (len(out_idx), B): exactly forward(u, steps)[out_idx] with u zero outside in_idx.
         float16 input runs the float16-deviation path and returns float32 (chessfly/brain.py:287-288)."""
+        if u_in.dim() != 2 or u_in.shape[0] != in_idx.numel():
+            raise ValueError(f"u_in must be (len(in_idx), B) = ({in_idx.numel()}, B), got {tuple(u_in.shape)}")
         _require_cuda(u_in, "u_in")
+        if u_in.device != self.pre.device or in_idx.device != self.pre.device or out_idx.device != self.pre.device:
+            raise RuntimeError(f"u_in, in_idx and out_idx must be on the module's device {self.pre.device}")
         if u_in.dtype not in (torch.float32, torch.float16):
             raise TypeError(f"alphafly_b200 computes in float32 or float16, got {u_in.dtype}")
         cone = self.light_cone(in_idx, out_idx, steps)

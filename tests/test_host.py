@@ -50,6 +50,19 @@ def test_cpu_tensors_are_rejected():
         rnn.edge_weights()
 
 
+def test_shapes_are_checked_before_any_device_work():
+    """A drive whose rows do not match in_idx (or the neuron count) is refused with ValueError, as the
+    reference's own indexing would refuse it (chessfly/brain.py:214, 271-275)."""
+    rnn = ConnectomeRNN(synth.tiny())
+    with pytest.raises(ValueError, match="len\\(in_idx\\)"):
+        rnn.forward_io(torch.zeros(4, 2), torch.arange(5), torch.arange(25, 30), 2)
+    with pytest.raises(ValueError, match="len\\(in_idx\\)"):
+        rnn.forward_io(torch.zeros(5), torch.arange(5), torch.arange(25, 30), 2)
+    with pytest.raises(ValueError, match="\\(N, B\\)"):
+        with torch.no_grad():
+            rnn(torch.zeros(29, 2), 2)
+
+
 def test_bench_algorithmic_bytes():
     import bench
     per_step, total = bench.algorithmic_bytes([0, 3, 4], [0, 0, 10], [0, 3, 0], batch=8, n_out=2)
