@@ -766,8 +766,9 @@ void launch(const StepArgs &args, cudaStream_t s) {
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
     // The ring kernel keeps gathers in flight across row ends, which pays on sub-matrices whose rows are
-    // shorter than half a 32-synapse window (measured on configuration 3: step 1, which has no synapses,
-    // 0.85 vs 1.04 ms); the register kernel wins on the others.  Both give bitwise the same results.
+    // shorter than half a 32-synapse window (configuration 3's steps 1 and 2: 0.85 vs 1.04 ms on step 1,
+    // which has no synapses, equal on step 2); the register kernel wins on the others.  Both give bitwise
+    // the same results.
     const bool ring = AFB_RING || a.nnz < kRingMaxDegree * (int64_t)a.n_rows;
     if (ring) {
         static unsigned long long configured = 0;   // devices on which this instantiation may use kRingBytes
