@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--batch", type=int, default=35_840, help="positions per GPU")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="positions per GPU (default 35,840; 2,048 with --train; 1,120 per round with --evaluator)")
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="CPU baseline sample budget")
     ap.add_argument("--no-e2e", action="store_true")
@@ -58,10 +59,8 @@ def parse():
     ap.add_argument("--evaluator", action="store_true",
                     help="time the self-play Evaluator (FlyChessNet rounds of --batch positions, 30 legal moves each)")
     args = ap.parse_args()
-    if args.train and args.batch == 35_840:
-        args.batch = 2048
-    if args.evaluator and args.batch == 35_840:
-        args.batch = 1120
+    if args.batch is None:
+        args.batch = 2048 if args.train else 1120 if args.evaluator else 35_840
     return args
 
 
