@@ -90,6 +90,19 @@ def losses(net: FlyChessNet, x, pi, legal, wdl, q, q_ratio: float):
     return policy_loss, value_loss, value_ce
 
 
+def grow_optimizer_state(opt_state: dict, opt: torch.optim.Optimizer) -> dict:
+    """An optimizer state saved before a parameter gained input columns (the encoder, when the attack
+    planes were added) made to fit the current parameters: each 2-D moment with the parameter's rows but
+    fewer columns is padded with zero columns (chessfly/train.py:211-218).  Returns the state it updated."""
+    params = [p for g in opt.param_groups for p in g["params"]]
+    for i, st in opt_state["state"].items():
+        p = params[i]
+        for k, v in list(st.items()):
+            if torch.is_tensor(v) and v.ndim == 2 and p.ndim == 2 and v.shape[0] == p.shape[0] and v.shape[1] < p.shape[1]:
+                st[k] = torch.cat([v, v.new_zeros(v.shape[0], p.shape[1] - v.shape[1])], dim=1)
+    return opt_state
+
+
 def average_gradients(params, group=None) -> None:
     """All-reduce (mean over ranks) the gradients of ``params`` through one flat buffer."""
     import torch.distributed as dist

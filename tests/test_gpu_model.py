@@ -246,3 +246,69 @@ def test_sharded_evaluator_equals_one_evaluator(small_net, lazy):
     finally:
         with torch.no_grad():
             small_net.brain.bias.sub_(0.2)
+
+
+def _tiny_net(**cfg):
+    return FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3, **cfg)).to(DEV)
+
+
+def test_factorised_policy_head_is_a_no_op_until_trained():
+    """tests/test_core.py:394-416: with the zero-initialised from/to terms the network is its dense policy
+    head on the normalised readout; an old checkpoint without those terms loads."""
+    from alphafly_b200.encoding import N_FEATURES
+    from alphafly_b200.model import load_weights
+    from alphafly_b200.encoding import N_BASE
+    net = _tiny_net()
+    with torch.no_grad():                                   # a trained dense head (the reference's is zero here)
+        net.policy.weight.normal_(0, 0.1, generator=torch.Generator(device=DEV).manual_seed(3))
+    old = {k: v for k, v in net.state_dict().items() if not k.startswith(("policy_from.", "policy_to."))}
+    load_weights(net, old)
+    x = torch.rand(3, N_FEATURES, generator=torch.Generator().manual_seed(0)).to(DEV)
+    net.infer_dtype = torch.float32
+    with torch.no_grad():
+        w, b = net.encoder.weight[:, :N_BASE], net.encoder.bias
+        u = ((x[:, :N_BASE] @ w.T + b) * net.cfg.input_gain).T.contiguous()
+        dense = net.policy(net.norm(net.brain.forward_io(u, net.in_idx, net.out_idx, 3).T))
+        assert float(dense.abs().max()) > 0
+        torch.testing.assert_close(net.eval()(x)[0], dense, rtol=1e-5, atol=1e-5)
+
+
+def test_attack_planes_are_invisible_unless_switched_on():
+    """tests/test_core.py:474-488 on the GPU: without attack_planes the features from N_BASE on change
+    nothing and their encoder columns get no gradient; with it they count."""
+    from alphafly_b200.encoding import N_BASE, N_FEATURES
+    g = torch.Generator().manual_seed(1)
+    off, on = _tiny_net().eval(), _tiny_net(attack_planes=True).eval()
+    with torch.no_grad():
+        off.encoder.weight[:, N_BASE:].copy_(torch.randn(off.encoder.weight[:, N_BASE:].shape, generator=g))
+        off.policy.weight.copy_(torch.randn(off.policy.weight.shape, generator=g) * 0.05)
+    on.load_state_dict(off.state_dict())
+    x = torch.rand(4, N_FEATURES, generator=g)
+    y = x.clone()
+    y[:, N_BASE:] = torch.rand(4, N_FEATURES - N_BASE, generator=g)
+    x, y = x.to(DEV), y.to(DEV)
+    with torch.no_grad():
+        torch.testing.assert_close(off(x)[0], off(y)[0], rtol=0, atol=0)
+        assert not torch.allclose(on(x)[0], on(y)[0])
+    off.train()
+    off(x)[0].sum().backward()
+    assert float(off.encoder.weight.grad[:, N_BASE:].abs().sum()) == 0
+
+
+def test_old_checkpoints_grow_the_encoder_without_changing_the_network():
+    """tests/test_core.py:451-471 (the network part): an 838-column encoder loads into an attack-plane
+    network as zero columns, so the new inputs change nothing until trained."""
+    from alphafly_b200.encoding import N_BASE, N_FEATURES
+    from alphafly_b200.model import load_weights
+    net = _tiny_net()
+    with torch.no_grad():
+        net.policy.weight.normal_(0, 0.05)
+    old = {k: (v[:, :N_BASE].clone() if k == "encoder.weight" else v.clone()) for k, v in net.state_dict().items()}
+    fresh = _tiny_net(attack_planes=True)
+    load_weights(fresh, old)
+    assert fresh.encoder.weight.shape[1] == N_FEATURES and float(fresh.encoder.weight[:, N_BASE:].abs().sum()) == 0
+    x = torch.rand(4, N_FEATURES, generator=torch.Generator().manual_seed(2)).to(DEV)
+    x_old = x.clone()
+    x_old[:, N_BASE:] = 0
+    with torch.no_grad():
+        torch.testing.assert_close(fresh.eval()(x)[0], fresh(x_old)[0])

@@ -50,3 +50,21 @@ def test_deepcopy_drops_native_handles_and_copies_parameters():
     assert c.brain._cone is None and net.brain._cone is not None
     for (k, a), (_, b) in zip(net.state_dict().items(), c.state_dict().items()):
         assert torch.equal(a, b) and (a.numel() == 0 or a.data_ptr() != b.data_ptr()), k
+
+
+def test_grow_optimizer_state_pads_the_encoder_moments():
+    """tests/test_core.py:451-471 (the optimizer part): Adam moments saved for an 838-column encoder are
+    padded with zero columns to the 967-column encoder, and the state loads."""
+    from alphafly_b200.train import TrainConfig, grow_optimizer_state, make_optimizer
+    fresh = FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3, attack_planes=True))
+    opt = make_optimizer(fresh, TrainConfig())
+    params = [p for g in opt.param_groups for p in g["params"]]
+    i = next(k for k, p in enumerate(params) if p is fresh.encoder.weight)
+    old_shape = (fresh.encoder.weight.shape[0], N_BASE)
+    state = {"state": {i: {"step": torch.tensor(5.0), "exp_avg": torch.ones(old_shape), "exp_avg_sq": torch.ones(old_shape)}},
+             "param_groups": opt.state_dict()["param_groups"]}
+    grown = grow_optimizer_state(state, opt)
+    st = grown["state"][i]
+    assert st["exp_avg"].shape == fresh.encoder.weight.shape and st["exp_avg_sq"].shape == fresh.encoder.weight.shape
+    assert float(st["exp_avg"][:, N_BASE:].abs().sum()) == 0 and float(st["exp_avg"][:, :N_BASE].sum()) == old_shape[0] * N_BASE
+    opt.load_state_dict(grown)
