@@ -147,6 +147,7 @@ class LightCone:
         self.out_src = self._export("out_src", 0, n_hit.value)
         self.out_idx = out_idx
         self.n_in, self.n_out = in_idx.numel(), out_idx.numel()
+        self.n = rnn.n
         self._weights: dict[int, tuple] = {}
 
     def _export(self, field: str, t: int, size: int) -> torch.Tensor:
@@ -185,6 +186,14 @@ class LightCone:
             h = float("inf") if h_max is None else float(h_max)
             _lib.check(self._lib.afb_cone_set_weights(self._h, mode, _ptr(w), _ptr(bias), _ptr(alpha_logit), h,
                                                       _stream(self.device)))
+
+    def resting(self, t: int) -> torch.Tensor:
+        """c_t, the resting trajectory (no position's input) after t steps, (N,) float32, for the weights of
+        the last ``set_weights`` (``afb_cone_resting``)."""
+        out = torch.empty(self.n, dtype=torch.float32, device=self.device)
+        with torch.cuda.device(self.device):
+            _lib.check(self._lib.afb_cone_resting(self._h, int(t), _ptr(out), _stream(self.device)))
+        return out
 
     def status(self, reset: bool = True) -> int:
         """Device status word of this cone's step kernels: 0 = ok, 1 = a bounded wait gave up (some
@@ -366,7 +375,7 @@ class ConnectomeRNN(nn.Module):
         new = self.__class__.__new__(self.__class__)
         memo[id(self)] = new
         for k, v in self.__dict__.items():
-            new.__dict__[k] = None if k in ("_cone", "_graph_cache", "_all_idx") else copy.deepcopy(v, memo)
+            new.__dict__[k] = None if k in ("_cone", "_graph_cache", "_all_idx", "_cached_f32") else copy.deepcopy(v, memo)
         return new
 
     # -- the literal recurrence ---------------------------------------------------------------------
@@ -417,6 +426,43 @@ class ConnectomeRNN(nn.Module):
         if getattr(self, "_cone", None) is None or self._cone[0] != key:
             self._cone = (key, LightCone(self, in_idx, out_idx, steps))
         return self._cone[1]
+
+    @property
+    def _cached(self):
+        """The float32 path's weight-dependent constants in the reference's layout, (key, (cs, ks, mats, alpha,
+        fused)), for diagnostics that read them (scripts/profile_gpu.py:27; built by chessfly/brain.py:296-305):
+        cs[t] the resting trajectory (N, 1), ks[t] the constant drive of R_t (|R_t|, 1), mats[t] the sub-matrix
+        W[R_t, R_{t-1}] as a sparse CSR tensor (None where the step has none), alpha (N, 1), fused[t] =
+        (carried, c_{t-1}[R_t], alpha[R_t]).  Made on demand for the light cone last used (the native
+        forward keeps its own constants); None before any light-cone forward."""
+        cone = getattr(self, "_cone", None)
+        if cone is None:
+            return None
+        cone = cone[1]
+        key = (self.log_gain._version, self.bias._version, self.alpha_logit._version, torch.float32, id(cone))
+        hit = getattr(self, "_cached_f32", None)
+        if hit is not None and hit[0] == key:
+            return hit
+        with torch.no_grad():
+            w = self.edge_weights()
+            cone.set_weights(self, _lib.MODE_F32, self._weight_key(_lib.MODE_F32, cone))
+            alpha = torch.sigmoid(self.alpha_logit).unsqueeze(1)
+            cs = [cone.resting(t).unsqueeze(1) for t in range(cone.steps + 1)]
+            full = self.csr(w)
+            ks, mats, fused = [None], [None], [None]
+            for t in range(1, cone.steps + 1):
+                rows, op = cone.rows[t], cone.ops[t]
+                drive = (full @ cs[t - 1] if t > 1 else torch.zeros_like(cs[0])) + self.bias.unsqueeze(1)
+                k = drive[rows]
+                mat = None
+                if op is not None:
+                    mat = op.csr(w[op.edges])
+                    k = k - mat @ cs[t - 1][cone.rows[t - 1]]
+                ks.append(k)
+                mats.append(mat)
+                fused.append((cone.carried[t].float(), cs[t - 1][rows].contiguous(), alpha[rows].contiguous()))
+        self._cached_f32 = (key, (cs, ks, mats, alpha, fused))
+        return self._cached_f32
 
     def _weight_key(self, mode, cone):
         return (self.log_gain._version, self.bias._version, self.alpha_logit._version, self.log_gain.data_ptr(),

@@ -277,3 +277,36 @@ def test_shuffled_control_batch_sweep(batch):
                              orc.sigmoid(inst.alpha_logit.numpy().astype(np.float64)), u.cpu().numpy().astype(np.float64))
         assert orc.rel_l2(out32.cpu().numpy(), ref) < F32_GATE
     assert rnn.device_status() == 0
+
+
+def test_cached_constants_in_the_reference_layout(small):
+    """brain._cached[1] = (cs, ks, mats, alpha, fused) as the reference's diagnostics read it
+    (scripts/profile_gpu.py:27): one float32 step rebuilt from them in the reference's way equals the
+    light-cone forward, and the resting trajectory equals the oracle's."""
+    inst, rnn = small
+    in_idx, out_idx = inst.in_idx.to(DEV), inst.out_idx.to(DEV)
+    u = torch.from_numpy(synth.drive(inst, 8, seed=2)).to(DEV)
+    with torch.no_grad():
+        out = rnn.forward_io(u, in_idx, out_idx, 6)
+        cs, ks, mats, alpha, fused = rnn._cached[1]
+        cone = rnn.light_cone(in_idx, out_idx, 6)
+        h = None
+        for t in range(1, 7):
+            rows = cone.rows[t]
+            x = ks[t].expand(-1, 8).clone() if mats[t] is None else mats[t] @ h + ks[t]
+            x = x.index_add(0, cone.u_pos[t], u[cone.u_src[t]]).clamp(0, rnn.h_max)
+            prev = cs[t - 1][rows].expand(-1, 8)
+            if len(cone.keep_next[t]):
+                prev = prev.index_copy(0, cone.keep_next[t], h[cone.keep_prev[t]])
+            h = torch.lerp(prev, x, alpha[rows])
+        rebuilt = cs[6][out_idx].expand(-1, 8).index_copy(0, cone.out_pos, h[cone.out_src])
+    assert orc.rel_l2(rebuilt.cpu().numpy(), out.cpu().numpy()) < 1e-5
+    pre, post = inst.conn.pre.numpy(), inst.conn.post.numpy()
+    w = orc.edge_weights(inst.conn.sign.numpy(), inst.w0.numpy(), inst.log_gain.numpy())
+    W = orc.full_csr(inst.n, pre, post)
+    c = np.zeros(inst.n)
+    a = orc.sigmoid(inst.alpha_logit.numpy().astype(np.float64))
+    for t in range(1, 7):
+        s = W.matmul(w, c[:, None])[:, 0] if t > 1 else np.zeros(inst.n)
+        c = orc.lerp(c, np.clip(s + inst.bias.numpy(), 0, 10.0), a)
+        assert orc.rel_l2(cs[t].squeeze(1).cpu().numpy(), c) < 1e-5, t
