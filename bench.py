@@ -66,10 +66,11 @@ def parse():
 
 def peaks():
     path = os.path.join(HERE, "MEASURED_PEAKS.json")
-    if os.path.exists(path):
-        d = json.load(open(path))
-        return float(d["hbm_gbs"]), "measured"
-    return 6650.0, "fallback"
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, ValueError, KeyError, TypeError):
+        return 6650.0, "fallback"
 
 
 def measured_traffic():
