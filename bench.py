@@ -258,6 +258,13 @@ def probe_arm(args):
         for bps in (2, 3, 4, 5, 6, 8):
             print(json.dumps({"probe": names[path], "warps_per_sm": 8 * bps, "slab_rows": rows,
                               "gbs": round(gather_ceiling(dev, rows, path=path, blocks_per_sm=bps), 1)}), flush=True)
+    for path, name in ((7, "ldg x8, 8-byte lanes"), (8, "ldg x16, 8-byte lanes")):   # 256-byte rows
+        for bps in (4, 5, 6, 8):
+            print(json.dumps({"probe": name, "warps_per_sm": 8 * bps, "slab_rows": rows,
+                              "gbs": round(gather_ceiling(dev, rows, path=path, blocks_per_sm=bps), 1)}), flush=True)
+    for slab in (32768, 83344, 124000, 166688, 250000):     # the step kernel's point: 40 warps, 4 loads in flight
+        print(json.dumps({"probe": names[5], "warps_per_sm": 40, "slab_rows": slab, "slab_mb": round(slab * 512 / 1e6, 1),
+                          "gbs": round(gather_ceiling(dev, slab, path=5, blocks_per_sm=5), 1)}), flush=True)
 
 
 def train_batch(inst, batch, seed):
