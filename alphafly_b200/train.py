@@ -5,9 +5,10 @@ groups, targets and losses: masked log-softmax policy cross-entropy, WDL cross-e
 mean-squared error of the expected value (``q_ratio``), gradient clipping at 5, AdamW.
 
 Data parallel (one process per GPU, NCCL): every rank evaluates its own positions; the gradients are
-averaged with one all-reduce of a flat buffer before clipping, and ``RunningNorm``'s batch statistics are
-combined exactly (sum and sum of squares over all ranks), so the ranks stay identical and the step
-equals the single-GPU step on the concatenated batch.
+averaged before clipping, in buckets that are all-reduced while the backward still runs
+(``BucketedAllReduce``), and ``RunningNorm``'s batch statistics are combined exactly (sum and sum of
+squares over all ranks), so the ranks stay identical and the step equals the single-GPU step on the
+concatenated batch.
 """
 
 from __future__ import annotations
@@ -118,10 +119,107 @@ def average_gradients(params, group=None) -> None:
         k += g.numel()
 
 
-def attach_data_parallel(net: FlyChessNet, group=None) -> None:
+class BucketedAllReduce:
+    """Gradient averaging over a process group, overlapped with the backward that produces the gradients.
+
+    ``params`` are taken in the order their gradients become ready and packed into buckets of about
+    ``bucket_mb`` MB (a larger parameter gets a bucket of its own).  Between ``arm()`` and ``finish()`` a
+    post-accumulate-grad hook counts each bucket's gradients; a complete bucket is flattened and all-reduced
+    asynchronously, so with NCCL its transfer runs on the communicator's stream while the rest of the
+    backward computes.  Buckets are launched strictly in bucket order (a complete bucket waits for the ones
+    before it), so every rank issues the same collectives in the same order.  ``finish()`` launches the
+    buckets the backward did not complete (parameters without a gradient take zeros and keep ``grad`` None),
+    waits, and writes the mean over ranks back into each ``grad``.  Outside an armed step the hooks do
+    nothing."""
+
+    def __init__(self, params, group=None, bucket_mb: float = 25.0):
+        self.group = group
+        self.buckets: list[list[torch.nn.Parameter]] = []
+        cap, cur, size = bucket_mb * 2**20, [], 0
+        for p in params:
+            nbytes = p.numel() * p.element_size()
+            if cur and size + nbytes > cap:
+                self.buckets.append(cur)
+                cur, size = [], 0
+            cur.append(p)
+            size += nbytes
+        if cur:
+            self.buckets.append(cur)
+        self._where = {id(p): k for k, b in enumerate(self.buckets) for p in b}
+        self._armed = False
+        self._hooks = [p.register_post_accumulate_grad_hook(self._on_grad) for b in self.buckets for p in b]
+        self.launched_in_backward = 0
+
+    def arm(self) -> None:
+        self._count = [0] * len(self.buckets)
+        self._pending: list = []               # (bucket, flat, work handle) in launch order
+        self._next = 0
+        self.launched_in_backward = 0
+        self._armed = True
+
+    def _on_grad(self, p: torch.Tensor) -> None:
+        if not self._armed:
+            return
+        k = self._where[id(p)]
+        self._count[k] += 1
+        launched = self._next
+        while self._next < len(self.buckets) and self._count[self._next] == len(self.buckets[self._next]):
+            self._launch(self._next)
+        self.launched_in_backward += self._next - launched
+
+    def _launch(self, k: int) -> None:
+        import torch.distributed as dist
+        flat = torch.cat([(p.grad if p.grad is not None else torch.zeros_like(p)).reshape(-1) for p in self.buckets[k]])
+        self._pending.append((k, flat, dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=self.group, async_op=True)))
+        self._next = k + 1
+
+    def finish(self) -> None:
+        import torch.distributed as dist
+        if not self._armed:
+            raise RuntimeError("finish() without arm()")
+        while self._next < len(self.buckets):
+            self._launch(self._next)
+        world = dist.get_world_size(self.group)
+        for k, flat, work in self._pending:
+            work.wait()
+            flat /= world
+            at = 0
+            for p in self.buckets[k]:
+                if p.grad is not None:
+                    p.grad.copy_(flat[at:at + p.numel()].view_as(p))
+                at += p.numel()
+        self._pending = []
+        self._armed = False
+
+    def __deepcopy__(self, memo):
+        return None           # hooks are not copied with the parameters: a copied network averages unbucketed
+
+    def remove(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
+
+
+def gradient_order(net: FlyChessNet) -> list[torch.nn.Parameter]:
+    """FlyChessNet's parameters in the order its backward produces their gradients: the heads, then the
+    connectome (one autograd node returns all three), then the input map."""
+    heads = [*net.policy_to.parameters(), *net.policy_from.parameters(), *net.value.parameters(),
+             *net.policy.parameters()]
+    order = heads + [net.brain.alpha_logit, net.brain.bias, net.brain.log_gain, *net.encoder.parameters()]
+    rest = [p for p in net.parameters() if all(p is not q for q in order)]
+    return order + rest
+
+
+def attach_data_parallel(net: FlyChessNet, group=None, bucket_mb: float = 25.0) -> None:
     """Make ``net.norm`` combine its batch statistics over the ranks of ``group`` (exactly: the statistics of
-    the concatenated batch)."""
+    the concatenated batch), and give ``net`` a ``BucketedAllReduce`` over its gradients, which
+    ``train_step(..., data_parallel=True)`` arms for each backward."""
     import torch.distributed as dist
+    if isinstance(net, torch.nn.Module):
+        if getattr(net, "grad_reducer", None) is not None:
+            net.grad_reducer.remove()
+        order = gradient_order(net) if isinstance(net, FlyChessNet) else list(net.parameters())[::-1]
+        net.grad_reducer = BucketedAllReduce(order, group, bucket_mb)
     norm = net.norm
 
     def sync_from_batch(r: torch.Tensor):
@@ -146,9 +244,17 @@ def train_step(net, opt, batch, device, q_ratio: float = 0.0, policy_target_offs
     x, pi, legal, wdl, q = collate(batch, device, policy_target_offset) if not isinstance(batch, tuple) else batch
     policy_loss, value_loss, value_ce = losses(net, x, pi, legal, wdl, q, q_ratio)
     opt.zero_grad(set_to_none=True)
-    (policy_loss + value_loss).backward()
-    if data_parallel:
-        average_gradients(net.parameters(), group)
+    reducer = getattr(net, "grad_reducer", None) if data_parallel else None
+    if reducer is not None and reducer.group is group:
+        reducer.arm()
+        try:
+            (policy_loss + value_loss).backward()
+        finally:
+            reducer.finish()
+    else:
+        (policy_loss + value_loss).backward()
+        if data_parallel:
+            average_gradients(net.parameters(), group)
     torch.nn.utils.clip_grad_norm_(net.parameters(), 5.0)
     opt.step()
     return {"policy_loss": policy_loss.item(), "value_loss": value_loss.item(), "value_ce": value_ce.item()}

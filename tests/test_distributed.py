@@ -1,5 +1,5 @@
 """Data-parallel host logic on CPU with the gloo backend, world size 2 (processes started with spawn):
-gradient averaging, RunningNorm statistics combined exactly over ranks, and a rank that leaves between
+gradient averaging (flat, and bucketed during the backward), RunningNorm statistics combined exactly over ranks, and a rank that leaves between
 steps surfacing as an error on the other rank instead of a hang."""
 
 import datetime
@@ -63,6 +63,54 @@ def test_gradient_average_and_exact_batch_statistics():
     for rank in range(2):
         torch.testing.assert_close(res[rank]["mean"], r.mean(0), rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(res[rank]["var"], r.var(0), rtol=1e-5, atol=1e-6)
+
+
+def _bucketed(rank, world, port, out):
+    _init(rank, world, port)
+    from alphafly_b200.train import BucketedAllReduce
+    torch.manual_seed(0)                                  # the same model on both ranks
+    net = torch.nn.Sequential(torch.nn.Linear(6, 40), torch.nn.Tanh(), torch.nn.Linear(40, 30), torch.nn.Tanh(),
+                              torch.nn.Linear(30, 2))
+    unused = torch.nn.Parameter(torch.zeros(4))           # takes no gradient
+    params = [p for m in reversed(net) for p in reversed(list(m.parameters()))] + [unused]
+    x = torch.randn(8, 6, generator=torch.Generator().manual_seed(20 + rank))
+    net(x).square().sum().backward()
+    local = [p.grad.clone() for p in params[:-1]]
+    for p in params[:-1]:
+        p.grad = None
+    red = BucketedAllReduce(params, bucket_mb=0.003)        # ~3 KB: several buckets
+    red.arm()
+    net(x).square().sum().backward()
+    in_backward = red.launched_in_backward
+    red.finish()
+    out[rank] = {"local": local, "avg": [p.grad.clone() for p in params[:-1]], "unused": unused.grad,
+                 "buckets": len(red.buckets), "in_backward": in_backward}
+    dist.destroy_process_group()
+
+
+def test_bucketed_all_reduce_overlaps_the_backward_and_averages():
+    port = _free_port()
+    with mp.Manager() as m:
+        out = m.dict()
+        mp.start_processes(_bucketed, args=(2, port, out), nprocs=2, start_method="spawn")
+        res = dict(out)
+    for rank in range(2):
+        r = res[rank]
+        assert r["buckets"] >= 3 and r["in_backward"] >= r["buckets"] - 1, r   # all but the unused one
+        assert r["unused"] is None
+        for k, g in enumerate(r["avg"]):
+            torch.testing.assert_close(g, (res[0]["local"][k] + res[1]["local"][k]) / 2)
+
+
+def test_gradient_order_covers_every_parameter_once():
+    from alphafly_b200 import synth
+    from alphafly_b200.model import FlyChessNet, ModelConfig
+    from alphafly_b200.train import gradient_order
+    net = FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3))
+    order = gradient_order(net)
+    assert len(order) == len(list(net.parameters()))
+    assert {id(p) for p in order} == {id(p) for p in net.parameters()}
+    assert order[-1] is net.encoder.bias or order[-1] is net.encoder.weight
 
 
 def _leaver(rank, world, port, out):

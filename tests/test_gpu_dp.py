@@ -21,7 +21,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _dp_rank(rank, world, port, out):
+def _dp_rank(rank, world, port, out, bucketed):
     import torch.distributed as dist
     from conftest import golden
     from alphafly_b200 import synth
@@ -35,15 +35,22 @@ def _dp_rank(rank, world, port, out):
     net = FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3))
     net.load_state_dict({k[len("state_"):]: torch.from_numpy(g[k]) for k in g.files if k.startswith("state_")})
     net = net.cuda().train()
-    attach_data_parallel(net)
+    attach_data_parallel(net, bucket_mb=0.02)    # ~20 KB buckets: several on the tiny network
     n = len(g["batch_x"])
     share = range(rank * n // world, (rank + 1) * n // world)
     batch = [Sample(g["batch_x"][i], g["batch_idx"][i].astype(np.int64), g["batch_pi"][i], float(g["batch_q"][i]),
                     int(g["batch_wdl"][i])) for i in share]
     x, pi, legal, wdl, q = collate(batch, "cuda")
     pl, vl, _ = losses(net, x, pi, legal, wdl, q, 0.5)
-    (pl + vl).backward()
-    average_gradients(net.parameters())
+    if bucketed:                                  # train_step's path: buckets all-reduced during the backward
+        red = net.grad_reducer
+        red.arm()
+        (pl + vl).backward()
+        out[f"in_backward{rank}"] = red.launched_in_backward
+        red.finish()
+    else:
+        (pl + vl).backward()
+        average_gradients(net.parameters())
     if rank == 0:
         out["grads"] = {k: p.grad.cpu() for k, p in net.named_parameters()}
         out["mean"], out["var"] = net.norm.mean.cpu(), net.norm.var.cpu()
@@ -52,12 +59,15 @@ def _dp_rank(rank, world, port, out):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_rank_gradients_equal_the_concatenated_batch():
+@pytest.mark.parametrize("bucketed", [False, True], ids=["flat", "bucketed"])
+def test_two_rank_gradients_equal_the_concatenated_batch(bucketed):
     from conftest import golden
     with mp.Manager() as m:
         out = m.dict()
-        mp.start_processes(_dp_rank, args=(2, _port(), out), nprocs=2, start_method="spawn")
+        mp.start_processes(_dp_rank, args=(2, _port(), out, bucketed), nprocs=2, start_method="spawn")
         res = dict(out)
+    if bucketed:                                  # the heads' and the connectome's buckets left before finish()
+        assert res["in_backward0"] >= 2 and res["in_backward1"] == res["in_backward0"], res
     g = golden("model")
     # the RunningNorm statistics equal the single-process statistics of the whole batch
     np.testing.assert_allclose(res["mean"].numpy(), g["norm_mean"], rtol=1e-5, atol=1e-6)
