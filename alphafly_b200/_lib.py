@@ -53,6 +53,7 @@ SIGNATURES = {
     "afb_graph_forward_workspace": (_sz, [_p, _i64]),
     "afb_graph_forward": (_int, [_p, _p, _p, _p, _f, _p, _i64, _i64, _int, _p, _i64, _p, _sz, _p]),
     "afb_legal_logits": (_int, [_i64, _p, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _p, _p, _p, _p, _p]),
+    "afb_input_map_f16": (_int, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _f, _p, _i64, _p, _p]),
     "afb_probe_gather_sink_words": (_i64, []),
     "afb_probe_gather": (_int, [_int, _int, _p, _i64, _p, _i64, _p, _i64, _p]),
 }

@@ -5,10 +5,11 @@
 
 ``FlyChessNet``, ``RunningNorm``, ``Evaluator``, ``ModelConfig``, ``load_weights`` and ``load_net`` keep the
 reference's names, parameters, buffers and state_dict keys (chessfly/model.py:26-161), so checkpoints
-load unchanged.  The recurrence runs in ``alphafly_b200.brain`` (libafb); the dense maps are plain
-GEMMs in cuBLAS through torch.  The input map writes the (sensory neurons, batch) layout the
-recurrence reads in one GEMM (W x^T scaled by the input gain), instead of x W^T followed by a
-transpose copy.
+load unchanged.  The recurrence runs in ``alphafly_b200.brain`` (libafb).  The input map writes the
+(sensory neurons, batch) layout the recurrence reads in one GEMM (W x^T scaled by the input gain),
+instead of x W^T followed by a transpose copy: for float16 inference in libafb's tensor-core kernel
+(``input_map_f16``), in float32 (training, the float32 path) through cuBLAS.  The heads are cuBLAS GEMMs,
+and the Evaluator's legal-move logits a libafb kernel.
 """
 
 from __future__ import annotations
@@ -93,14 +94,14 @@ class FlyChessNet(nn.Module):
     def drive(self, x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
         """u_in (sensory neurons, batch) = input_gain * (W x^T + b), over the first N_BASE features unless
         the attack planes are switched on (chessfly/model.py:98-102).  For the float16 inference path the
-        product runs on the tensor cores: float16 weights (a copy refreshed when the encoder changes) times
-        the float16 features (board bits, exact), accumulated in float32 and rounded once to the float16
-        drive the deviation path reads; everything else is float32 as in the reference."""
+        product runs on the tensor cores (``input_map_f16``): float16 weights (a copy refreshed when the
+        encoder changes) times the float16 features (board bits, exact), accumulated in float32 and rounded
+        once to the float16 drive the deviation path reads; everything else is float32 as in the reference."""
         k = N_FEATURES if self.cfg.attack_planes else N_BASE
         g = self.cfg.input_gain
         if dtype == torch.float16 and x.is_cuda and not torch.is_grad_enabled():
             w16, b16 = self.half_encoder()
-            return torch.addmm(b16.unsqueeze(1), w16, x[:, :k].half().T, beta=g, alpha=g)
+            return input_map_f16(w16, b16, x[:, :k], g, self._map_status(x.device))
         w, b = self.encoder.weight[:, :k], self.encoder.bias
         u = torch.addmm(b.unsqueeze(1), w, x[:, :k].float().T, beta=g, alpha=g)
         return u.to(dtype).contiguous()
@@ -115,13 +116,22 @@ class FlyChessNet(nn.Module):
         where = (w.data_ptr(), b.data_ptr(), k)
         c = getattr(self, "_enc16", None)
         if c is None or c[1] != where:
-            c = [key, where, w[:, :k].half().contiguous(), b.half()]
+            w16 = torch.zeros(w.shape[0], -(-k // 8) * 8, dtype=torch.float16, device=w.device)[:, :k]   # rows on 16 B
+            w16.copy_(w[:, :k])
+            c = [key, where, w16, b.half()]
             self._enc16 = c
         elif c[0] != key:
             c[2].copy_(w[:, :k])
             c[3].copy_(b)
             c[0] = key
         return c[2], c[3]
+
+    def _map_status(self, device) -> torch.Tensor:
+        """The input map's device status word on ``device`` (0 = ok; set when a bounded wait gave up)."""
+        st = getattr(self, "_status", None)
+        if st is None or st.device != device:
+            st = self._status = torch.zeros(1, dtype=torch.int32, device=device)
+        return st
 
     def readout(self, x: torch.Tensor) -> torch.Tensor:
         """x: (B, N_FEATURES) -> the normalised output-neuron state r (B, len(out_idx)) the heads read
@@ -140,6 +150,32 @@ class FlyChessNet(nn.Module):
     def expected_value(wdl_logits: torch.Tensor) -> torch.Tensor:
         p = wdl_logits.softmax(-1)
         return p[..., 0] - p[..., 2]
+
+
+def input_map_f16(w16: torch.Tensor, b16: torch.Tensor, x: torch.Tensor, gain: float,
+                  status: torch.Tensor | None = None) -> torch.Tensor:
+    """u (n_in, B) float16 = fp16(gain * (w16 x^T + b16)) by the library's tensor-core kernel
+    (``afb_input_map_f16``; chessfly/model.py:101-102 with the float16 cast).  w16 (n_in, k) and x (B, k)
+    float16 with unit column stride; rows of x that do not start on 16 bytes are copied first.  The result
+    is a view with a row stride rounded up to 8 positions (the light-cone forward reads it as it is)."""
+    n_in, k = w16.shape
+    if w16.stride(1) != 1 or w16.stride(0) % 8 or w16.data_ptr() % 16:
+        raise ValueError("w16 rows must be contiguous and start on 16-byte boundaries")
+    if x.shape[1] != k:
+        raise ValueError(f"x has {x.shape[1]} features, the map takes {k}")
+    if x.dtype != torch.float16 or x.stride(1) != 1 or x.stride(0) % 8 or x.data_ptr() % 16:
+        xp = torch.empty(x.shape[0], -(-k // 8) * 8, dtype=torch.float16, device=x.device)[:, :k]
+        xp.copy_(x)
+        x = xp
+    batch = x.shape[0]
+    ldu = -(-batch // 8) * 8
+    u = torch.empty(n_in, ldu, dtype=torch.float16, device=x.device)[:, :batch]
+    lib = _lib.load()
+    _lib.check(lib.afb_input_map_f16(n_in, batch, k, w16.data_ptr(), w16.stride(0), x.data_ptr(), x.stride(0),
+                                     b16.data_ptr(), float(gain), u.data_ptr(), ldu,
+                                     status.data_ptr() if status is not None else None,
+                                     torch.cuda.current_stream(x.device).cuda_stream))
+    return u
 
 
 class _Handle:
@@ -226,7 +262,8 @@ class Evaluator:
             return entry
         while len(self._graphs) >= self.max_graphs:
             self._graphs.popitem(last=False)
-        x = torch.zeros(bucket, N_FEATURES, dtype=torch.float16, device=self.device)
+        # rows padded to 16 bytes, so the input map's TMA reads them in place
+        x = torch.zeros(bucket, -(-N_FEATURES // 8) * 8, dtype=torch.float16, device=self.device)[:, :N_FEATURES]
         side = torch.cuda.Stream(self.device)
         side.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(side):                  # warm-up: cone, constants, library handles

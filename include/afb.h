@@ -191,6 +191,18 @@ AFB_API int afb_legal_logits(int64_t m, const int64_t *rows, const int64_t *cols
                              const float *f, const float *t, const int64_t *move_from, const int64_t *move_to,
                              float *out, void *stream);
 
+/* ---- the float16 input map (chessfly/model.py:101-102) ----------------------------------------------
+ * The reference computes the drive of the input neurons as  u_in = (x[:, :k] W^T + b) * input_gain,
+ * transposed to (n_in, B) and cast to float16 for the deviation path.  This entry point computes
+ *     u[i * ldu + p] = fp16( gain * (sum_{k < k_dim} w[i * ldw + k] x[p * ldx + k] + b[i]) )
+ * for i < n_in, p < batch on the tensor cores (tcgen05.mma, float16 operands, float32 accumulation, one
+ * rounding).  w (n_in rows) and x (batch rows) are float16, row-major with k_dim valid elements per row;
+ * ldw and ldx must be multiples of 8 and w, x 16-byte aligned (TMA operands).  b: n_in float16.  u: float16,
+ * ldu >= batch (any; multiples of 8 take the vector stores).  status: optional device int, OR-ed with a
+ * non-zero code if one of the kernel's bounded waits gave up (never expected).  Asynchronous on `stream`. */
+AFB_API int afb_input_map_f16(int64_t n_in, int64_t batch, int64_t k_dim, const void *w, int64_t ldw, const void *x,
+                              int64_t ldx, const void *b, float gain, void *u, int64_t ldu, int *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,3 +41,18 @@ def test_argument_errors_are_reported_without_a_gpu():
     assert lib.afb_cone_forward_workspace(None, 0, 64) == 0
     with pytest.raises(_lib.AfbError, match="unknown mode"):
         _lib.check(lib.afb_cone_forward(ctypes.c_void_p(16), 7, None, 0, 0, None, 0, None, 0, None))
+
+
+def test_input_map_argument_errors_without_a_gpu():
+    from alphafly_b200 import _lib
+    lib = _lib.load()
+    p = ctypes.c_void_p(256)
+    assert lib.afb_input_map_f16(0, 64, 838, p, 840, p, 840, p, 5.0, p, 64, None, None) == _lib.OK   # nothing to do
+    with pytest.raises(_lib.AfbError, match="negative size"):
+        _lib.check(lib.afb_input_map_f16(-1, 64, 838, p, 840, p, 840, p, 5.0, p, 64, None, None))
+    with pytest.raises(_lib.AfbError, match="multiple of 8"):
+        _lib.check(lib.afb_input_map_f16(10, 64, 838, p, 838, p, 840, p, 5.0, p, 64, None, None))
+    with pytest.raises(_lib.AfbError, match="below the row length"):
+        _lib.check(lib.afb_input_map_f16(10, 64, 838, p, 840, p, 840, p, 5.0, p, 32, None, None))
+    with pytest.raises(_lib.AfbError, match="16-byte aligned"):
+        _lib.check(lib.afb_input_map_f16(10, 64, 838, ctypes.c_void_p(258), 840, p, 840, p, 5.0, p, 64, None, None))

@@ -192,6 +192,41 @@ def test_legal_logits_kernel_against_torch():
     assert float((out[ok].double() - ref).abs().max()) < 1e-4
 
 
+def _padded_half(a: torch.Tensor) -> torch.Tensor:
+    rows, k = a.shape
+    out = torch.zeros(rows, -(-k // 8) * 8, dtype=torch.float16, device=DEV)[:, :k]
+    out.copy_(a)
+    return out
+
+
+@pytest.mark.parametrize("n_in,batch,k", [(17937, 1120, 838), (300, 1, 838), (129, 257, 967), (128, 256, 64),
+                                          (5, 300, 8), (200, 37, 100), (1000, 4096, 838)])
+def test_input_map_kernel_against_float32(n_in, batch, k):
+    """The tcgen05 input map against a float32 product of the same float16 operands: within the one
+    float16 rounding of the result.  Ragged tiles in every dimension, k below, at and above one k-block."""
+    from alphafly_b200.model import input_map_f16
+    g = torch.Generator().manual_seed(n_in * 7 + batch * 3 + k)
+    w16 = _padded_half(torch.randn(n_in, k, generator=g) * 0.05)
+    b16 = (torch.randn(n_in, generator=g) * 0.3).half().to(DEV)
+    feats = (torch.rand(batch, k, generator=g) < 0.06).half()       # board bits, exact in float16
+    x = feats.to(DEV)                                                # row stride k: copied to 16-byte rows
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    u = input_map_f16(w16, b16, x, 5.0, status)
+    ref = 5.0 * (w16.float().cpu() @ feats.float().T + b16.float().cpu()[:, None])
+    assert u.shape == (n_in, batch) and u.dtype == torch.float16 and u.stride(1) == 1
+    torch.testing.assert_close(u.float().cpu(), ref, rtol=2 ** -10, atol=1e-5)
+    # the same through the C entry point with an unaligned row stride (scalar stores)
+    from alphafly_b200 import _lib
+    xp = _padded_half(x)
+    u2 = torch.full((n_in, batch + 1), float("nan"), dtype=torch.float16, device=DEV)
+    _lib.check(_lib.load().afb_input_map_f16(n_in, batch, k, w16.data_ptr(), w16.stride(0), xp.data_ptr(), xp.stride(0),
+                                             b16.data_ptr(), 5.0, u2.data_ptr(), batch + 1, status.data_ptr(),
+                                             torch.cuda.current_stream().cuda_stream))
+    assert torch.equal(u2[:, :batch], u)
+    assert torch.isnan(u2[:, batch]).all()                           # nothing written past the batch
+    assert int(status.item()) == 0
+
+
 def test_web_model_round_trip_evaluates_like_the_exported_network(small_net, tmp_path):
     """export_web_model -> net_from_web_model on configuration 1's network: the manifest's test vectors
     (float32 logits of legal moves and values, made on the original network) are reproduced by the rebuilt
