@@ -16,10 +16,14 @@
 //     k-block into TMEM; tcgen05.commit frees the stage when its MMAs have read it, and after the last
 //     k-block signals the accumulator barrier.
 //   - all 4 warps: epilogue.  Warp w reads TMEM lanes 32w..32w+31 (its rows) 32 columns at a time with
-//     tcgen05.ld, applies the gain and the bias in float32, rounds once to float16 and stores.
+//     tcgen05.ld, applies the gain and the bias in float32 and rounds once to float16.  The 128 x 32
+//     chunks are staged in the (now idle) operand ring, SWIZZLE_64B, and written by TMA bulk stores, so
+//     the global writes are whole lines; a u whose rows do not start on 16 bytes takes scalar stores.
 // Every mbarrier wait is bounded: a wait that gives up sets *status (the host reads it) and the CTA
 // skips ahead instead of hanging; TMEM is always released.  No cluster, no multicast.
 #include <cudaTypedefs.h>
+
+#include <cstring>
 
 #include "common.cuh"
 
@@ -73,10 +77,20 @@ __device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap *map, i
                  ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
 }
 
+__device__ __forceinline__ void tma_store(const CUtensorMap *map, int x, int y, uint32_t src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n"
+                 ::"l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(src) : "memory");
+}
+
+constexpr int kChunkCols = 32;                         // one tcgen05.ld of 32 columns = one TMA store box
+constexpr int kChunkBytes = kBM * kChunkCols * 2;      // 8 KB staged per chunk
+static_assert(kBN / kChunkCols * kChunkBytes <= kStages * kStageBytes, "the staged tile must fit in the operand ring");
+
 __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_constant__ CUtensorMap map_w,
-                                                             const __grid_constant__ CUtensorMap map_x, int n_in,
+                                                             const __grid_constant__ CUtensorMap map_x,
+                                                             const __grid_constant__ CUtensorMap map_u, int n_in,
                                                              int batch, int k_dim, const __half *__restrict__ bias,
-                                                             float gain, __half *__restrict__ u, int64_t ldu, int u_vec,
+                                                             float gain, __half *__restrict__ u, int64_t ldu, int tma_out,
                                                              int *__restrict__ status) {
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = (uint32_t)__cvta_generic_to_shared(smem_raw);
@@ -151,15 +165,16 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
     __syncwarp();
 
     // epilogue: every thread owns one row (neuron) of the tile
-    const bool acc_ok = bar_wait(acc_bar, 0);
-    if (!acc_ok && lane == 0) fail(status, 4);
+    const bool acc_ok = __syncthreads_and(bar_wait(acc_bar, 0)) != 0;   // the same answer in every thread
+    if (!acc_ok && threadIdx.x == 0) fail(status, 4);
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    const int m = m0 + warp * 32 + lane;
+    const int row = warp * 32 + lane, m = m0 + row;
     const float gb = m < n_in ? gain * __half2float(bias[m]) : 0.f;
     __half *const urow = u + (int64_t)(m < n_in ? m : 0) * ldu;
+    const bool staged = tma_out && acc_ok;                               // every MMA is done: the ring is free
 #pragma unroll 1
-    for (int c = 0; c < kBN / 32; ++c) {
-        const int n = n0 + c * 32;
+    for (int c = 0; c < kBN / kChunkCols; ++c) {
+        const int n = n0 + c * kChunkCols;
         if (n >= batch) break;                                           // uniform over the CTA
         uint32_t r[32];
         const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32);
@@ -171,21 +186,36 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
                        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
                      : "r"(taddr));
         asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-        if (m >= n_in || !acc_ok) continue;
-        uint32_t h[16];
+        if (staged) {
+            // row `row` of chunk c: 64 bytes at c*8K + row*64, its 16-byte pieces in SWIZZLE_64B order
+            // (piece q at q ^ ((row >> 1) & 3), the pattern the TMA store un-swizzles)
+            const uint32_t dst = tiles + c * kChunkBytes + row * 64;
 #pragma unroll
-        for (int q = 0; q < 16; ++q) {
-            const __half2 v = __floats2half2_rn(fmaf(gain, __uint_as_float(r[2 * q]), gb), fmaf(gain, __uint_as_float(r[2 * q + 1]), gb));
-            h[q] = *reinterpret_cast<const uint32_t *>(&v);
-        }
-        if (u_vec && n + 32 <= batch) {
-            uint4 *dst = reinterpret_cast<uint4 *>(urow + n);
+            for (int q = 0; q < 4; ++q) {
+                uint32_t h[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-        } else {
+                for (int e = 0; e < 4; ++e) {
+                    const int j = 8 * q + 2 * e;
+                    const __half2 v = __floats2half2_rn(fmaf(gain, __uint_as_float(r[j]), gb), fmaf(gain, __uint_as_float(r[j + 1]), gb));
+                    h[e] = *reinterpret_cast<const uint32_t *>(&v);
+                }
+                asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};\n" ::"r"(dst + ((q ^ ((row >> 1) & 3)) << 4)), "r"(h[0]),
+                             "r"(h[1]), "r"(h[2]), "r"(h[3]) : "memory");
+            }
+        } else if (m < n_in && acc_ok) {
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
+            for (int j = 0; j < kChunkCols; ++j)
                 if (n + j < batch) urow[n + j] = __float2half_rn(fmaf(gain, __uint_as_float(r[j]), gb));
+        }
+    }
+    if (staged) {
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // the staged chunks, visible to TMA
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            for (int c = 0; c < kBN / kChunkCols && n0 + c * kChunkCols < batch; ++c)
+                tma_store(&map_u, n0 + c * kChunkCols, m0, tiles + c * kChunkBytes);     // rows / columns past u: clipped
+            asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");         // smem read before the CTA exits
         }
     }
     asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory");
@@ -220,6 +250,19 @@ void encode_operand(CUtensorMap *map, const void *base, int64_t rows, int64_t k_
     AFB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
 }
 
+// The output u: n_in rows x batch float16 columns, row stride ldu elements, boxes of 128 rows x 32 columns
+// staged SWIZZLE_64B.
+void encode_output(CUtensorMap *map, void *base, int64_t n_in, int64_t batch, int64_t ldu) {
+    const cuuint64_t dim[2] = {(cuuint64_t)batch, (cuuint64_t)n_in};
+    const cuuint64_t stride[1] = {(cuuint64_t)ldu * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kChunkCols, (cuuint32_t)kBM};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dim, stride, box, estride,
+                                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AFB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output) failed with code " + std::to_string((int)r));
+}
+
 }  // namespace
 }  // namespace afb
 
@@ -237,10 +280,12 @@ extern "C" int afb_input_map_f16(int64_t n_in, int64_t batch, int64_t k_dim, con
         AFB_CHECK(ldw % 8 == 0 && ldx % 8 == 0, "W and x rows must start on 16-byte boundaries (leading dimension a multiple of 8)");
         AFB_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
                   "W and x must be 16-byte aligned");
-        CUtensorMap map_w, map_x;
+        CUtensorMap map_w, map_x, map_u;
         encode_operand(&map_w, w, n_in, k_dim, ldw, kBM);
         encode_operand(&map_x, x, batch, k_dim, ldx, kBN);
-        const int u_vec = (ldu % 8 == 0 && (reinterpret_cast<uintptr_t>(u) & 15) == 0) ? 1 : 0;
+        const int tma_out = (ldu % 8 == 0 && (reinterpret_cast<uintptr_t>(u) & 15) == 0) ? 1 : 0;
+        if (tma_out) encode_output(&map_u, u, n_in, batch, ldu);
+        else std::memset(&map_u, 0, sizeof(map_u));
         static bool configured[64] = {false};
         int dev = 0;
         AFB_CUDA(cudaGetDevice(&dev));
@@ -250,9 +295,9 @@ extern "C" int afb_input_map_f16(int64_t n_in, int64_t batch, int64_t k_dim, con
         }
         const dim3 grid((unsigned)((n_in + kBM - 1) / kBM), (unsigned)((batch + kBN - 1) / kBN));
         AFB_CHECK(grid.y < 65536, "batch too large for one launch");
-        input_map_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(map_w, map_x, (int)n_in, (int)batch, (int)k_dim,
-                                                                               static_cast<const __half *>(bias), gain,
-                                                                               static_cast<__half *>(u), ldu, u_vec, status);
+        input_map_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(map_w, map_x, map_u, (int)n_in, (int)batch,
+                                                                               (int)k_dim, static_cast<const __half *>(bias), gain,
+                                                                               static_cast<__half *>(u), ldu, tma_out, status);
         AFB_LAUNCHED();
     });
 }

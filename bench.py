@@ -58,6 +58,8 @@ def parse():
                     help="time configurations 1, 2 and 4 (the other workloads of the scope; one JSON line each)")
     ap.add_argument("--evaluator", action="store_true",
                     help="time the self-play Evaluator (FlyChessNet rounds of --batch positions, 30 legal moves each)")
+    ap.add_argument("--inmap", action="store_true",
+                    help="time the float16 input map (tcgen05 kernel) against cuBLAS on the same operands")
     args = ap.parse_args()
     if args.batch is None:
         args.batch = 2048 if args.train else 1120 if args.evaluator else 35_840
@@ -71,6 +73,16 @@ def peaks():
             return float(json.load(f)["hbm_gbs"]), "measured"
     except (OSError, ValueError, KeyError, TypeError):
         return 6650.0, "fallback"
+
+
+def tensor_peak():
+    """Dense bf16 (= float16) tensor throughput in TFLOP/s: the burst figure of MEASURED_PEAKS.json, else the
+    earlier measurement on this pool."""
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops"]), "measured"
+    except (OSError, ValueError, KeyError, TypeError):
+        return 1590.0, "fallback"
 
 
 def measured_traffic():
@@ -265,6 +277,59 @@ def probe_arm(args):
     for slab in (32768, 83344, 124000, 166688, 250000):     # the step kernel's point: 40 warps, 4 loads in flight
         print(json.dumps({"probe": names[5], "warps_per_sm": 40, "slab_rows": slab, "slab_mb": round(slab * 512 / 1e6, 1),
                           "gbs": round(gather_ceiling(dev, slab, path=5, blocks_per_sm=5), 1)}), flush=True)
+
+
+def inmap_arm(args):
+    """The float16 input map alone: afb_input_map_f16 (tcgen05 + TMA) against torch's cuBLAS addmm on the
+    same float16 operands, u = 5 (W x^T + b) for 17,937 sensory neurons from 838 board features, at the
+    Evaluator's round (1,120 positions) and up to configuration 3's batch.  L2 is flushed (a 256 MB write)
+    before every timed launch; each launch is timed alone with CUDA events on the launching stream."""
+    from alphafly_b200 import _lib
+    from alphafly_b200.model import input_map_f16
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n_in, k, gain = 17_937, 838, 5.0
+    g = torch.Generator().manual_seed(5)
+    w16 = torch.zeros(n_in, 840, dtype=torch.float16, device=dev)[:, :k]
+    w16.copy_(torch.randn(n_in, k, generator=g) * 0.05)
+    b16 = (torch.randn(n_in, generator=g) * 0.3).half().to(dev)
+    flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    peak, peak_kind = tensor_peak()
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, reps):
+        total = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            fn()
+            b.record(stream)
+            b.synchronize()
+            total += a.elapsed_time(b)
+        return total / reps
+
+    for batch in sorted({1120, 8192, args.batch}):
+        x = torch.zeros(batch, 840, dtype=torch.float16, device=dev)[:, :k]
+        x.copy_((torch.rand(batch, k, generator=g) < 0.06).half())
+        out = {}
+        fns = {"tcgen05": lambda: out.__setitem__("ours", input_map_f16(w16, b16, x, gain, status)),
+               "cublas": lambda: out.__setitem__("cublas", torch.addmm(b16.unsqueeze(1), w16, x.T, beta=gain, alpha=gain))}
+        for fn in fns.values():
+            for _ in range(args.warmup):
+                fn()
+        ms = {name: timed(fn, max(args.steps, 3)) for name, fn in fns.items()}
+        torch.cuda.synchronize(dev)
+        _lib.check(0 if int(status.item()) == 0 else _lib.ECUDA)
+        flops = 2.0 * n_in * k * batch
+        diff = float((out["ours"].float() - out["cublas"].float()).abs().max())
+        print(json.dumps({"kernel": "input_map_kernel (tcgen05.mma 128x256x16 f16->f32, TMA SWIZZLE_128B)",
+                          "workload": f"drive of {n_in} sensory neurons from {k} features", "batch": batch,
+                          "ms": round(ms["tcgen05"], 4), "tflops": round(flops / ms["tcgen05"] / 1e9, 1),
+                          "frac": round(flops / ms["tcgen05"] / 1e9 / peak, 3), "peak_tflops": peak, "peak": peak_kind,
+                          "cublas_ms": round(ms["cublas"], 4), "cublas_tflops": round(flops / ms["cublas"] / 1e9, 1),
+                          "max_abs_diff_vs_cublas": diff, "l2": "flushed before every launch"}), flush=True)
 
 
 def train_batch(inst, batch, seed):
@@ -481,6 +546,8 @@ def main():
         return reference_arm(args, rank, world)
     if args.probe:
         return probe_arm(args)
+    if args.inmap:
+        return inmap_arm(args)
     if args.train:
         return train_arm(args, rank, world, local)
     if args.evaluator:
