@@ -6,19 +6,21 @@
 // (rows of k_dim elements, row strides multiples of 8 elements); u is written neuron-major (n_in x ldu),
 // the layout the light-cone forward reads its drive in.
 //
-// One CTA computes a 128 x 256 tile of u (128 neurons = the 128 TMEM lanes, 256 positions = 256 TMEM
-// columns of float32 accumulators):
-//   - warp 0, one lane: TMA producer.  Each k-block is a 128 x 64 tile of W and a 256 x 64 tile of x
-//     (128 bytes per row, SWIZZLE_128B), loaded by cp.async.bulk.tensor into a ring of kStages stages;
-//     an mbarrier per stage counts the bytes in.  Columns past k_dim, and rows past n_in or batch, are
-//     zero-filled by the TMA unit.
-//   - warp 1, one lane: MMA issuer.  Four tcgen05.mma (M 128, N 256, K 16, float16 in, float32 out) per
+// One CTA computes a (kSub x 128) x 256 tile of u: kSub MMA tiles of 128 neurons (the 128 TMEM lanes) by
+// 256 positions, their float32 accumulators side by side in TMEM (kSub x 256 columns).  Two sub-tiles
+// share every x tile, which cuts the L2 -> SM bytes per FLOP by a third against one.
+//   - warp 0, one lane: TMA producer.  Each k-block is a (kSub x 128) x 64 tile of W and a 256 x 64 tile
+//     of x (128 bytes per row, SWIZZLE_128B), loaded by cp.async.bulk.tensor into a ring of kStages
+//     stages; an mbarrier per stage counts the bytes in.  Columns past k_dim, and rows past n_in or
+//     batch, are zero-filled by the TMA unit.
+//   - warp 1, one lane: MMA issuer.  4 x kSub tcgen05.mma (M 128, N 256, K 16, float16 in, float32 out) per
 //     k-block into TMEM; tcgen05.commit frees the stage when its MMAs have read it, and after the last
 //     k-block signals the accumulator barrier.
-//   - all 4 warps: epilogue.  Warp w reads TMEM lanes 32w..32w+31 (its rows) 32 columns at a time with
-//     tcgen05.ld, applies the gain and the bias in float32 and rounds once to float16.  The 128 x 32
-//     chunks are staged in the (now idle) operand ring, SWIZZLE_64B, and written by TMA bulk stores, so
-//     the global writes are whole lines; a u whose rows do not start on 16 bytes takes scalar stores.
+//   - all warps: epilogue.  Warp w reads TMEM lanes 32(w%4)..32(w%4)+31 of sub-tile w/4 32 columns at a
+//     time with tcgen05.ld, applies the gain and the bias in float32 and rounds once to float16.  The
+//     128 x 32 chunks are staged in the (now idle) operand ring, SWIZZLE_64B, and written by TMA bulk
+//     stores, so the global writes are whole lines; a u whose rows do not start on 16 bytes takes scalar
+//     stores.
 // Every mbarrier wait is bounded: a wait that gives up sets *status (the host reads it) and the CTA
 // skips ahead instead of hanging; TMEM is always released.  No cluster, no multicast.
 #include <cudaTypedefs.h>
@@ -30,17 +32,24 @@
 namespace afb {
 namespace {
 
-constexpr int kBM = 128;                        // neurons per CTA (TMEM lanes)
-constexpr int kBN = 256;                        // positions per CTA (TMEM columns)
+#ifndef AFB_INMAP_SUB
+#define AFB_INMAP_SUB 2
+#endif
+constexpr int kBM = 128;                        // neurons per MMA (TMEM lanes)
+constexpr int kSub = AFB_INMAP_SUB;             // MMA tiles per CTA along the neurons
+constexpr int kRows = kSub * kBM;               // neurons per CTA
+constexpr int kBN = 256;                        // positions per CTA (TMEM columns per sub-tile)
 constexpr int kBK = 64;                         // 64 float16 = one 128-byte swizzle row
 constexpr int kMmaK = 16;                       // K of one tcgen05.mma kind::f16
-constexpr int kStages = 2;                      // two CTAs per SM overlap one's epilogue with the other's loads
-constexpr int kThreads = 128;
-constexpr int kABytes = kBM * kBK * 2;          // 16 KB
+// one CTA per SM with two sub-tiles (3 stages of 64 KB); with one, two CTAs per SM of 2 stages of 48 KB
+constexpr int kStages = kSub == 2 ? 3 : 2;
+constexpr int kThreads = 128 * kSub;            // one epilogue warp per (TMEM lane quarter, sub-tile)
+constexpr int kABytes = kRows * kBK * 2;        // 16 KB per sub-tile
 constexpr int kBBytes = kBN * kBK * 2;          // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
+constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* barriers */ + 1024 /* alignment slack */;
-constexpr uint32_t kTmemCols = kBN;             // float32 accumulators: one column per position
+constexpr uint32_t kTmemCols = kSub * kBN;      // float32 accumulators: one column per position and sub-tile
+static_assert(kSub == 1 || kSub == 2, "one or two MMA tiles per CTA");
 constexpr uint32_t kWaitLimit = 1u << 22;
 
 // Instruction descriptor of tcgen05.mma kind::f16: D float32 (bits 4-5 = 1), A and B float16 (bits 7-9,
@@ -84,9 +93,9 @@ __device__ __forceinline__ void tma_store(const CUtensorMap *map, int x, int y, 
 
 constexpr int kChunkCols = 32;                         // one tcgen05.ld of 32 columns = one TMA store box
 constexpr int kChunkBytes = kBM * kChunkCols * 2;      // 8 KB staged per chunk
-static_assert(kBN / kChunkCols * kChunkBytes <= kStages * kStageBytes, "the staged tile must fit in the operand ring");
+static_assert(kSub * (kBN / kChunkCols) * kChunkBytes <= kStages * kStageBytes, "the staged tile must fit in the operand ring");
 
-__global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_constant__ CUtensorMap map_w,
+__global__ void __launch_bounds__(kThreads, 1) input_map_kernel(const __grid_constant__ CUtensorMap map_w,
                                                              const __grid_constant__ CUtensorMap map_x,
                                                              const __grid_constant__ CUtensorMap map_u, int n_in,
                                                              int batch, int k_dim, const __half *__restrict__ bias,
@@ -94,7 +103,7 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
                                                              int *__restrict__ status) {
     extern __shared__ unsigned char smem_raw[];
     const uint32_t raw = (uint32_t)__cvta_generic_to_shared(smem_raw);
-    const uint32_t tiles = (raw + 1023u) & ~1023u;                       // stage s: A at +s*48K, B at +s*48K+16K
+    const uint32_t tiles = (raw + 1023u) & ~1023u;                       // stage s at +s*kStageBytes: W tile, then x tile
     const uint32_t bars = tiles + kStages * kStageBytes;                 // full[s], empty[s], acc, tmem slot
     auto full = [&](int s) { return bars + 8u * s; };
     auto empty = [&](int s) { return bars + 8u * (kStages + s); };
@@ -103,7 +112,7 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
     unsigned char *const slot_ptr = smem_raw + (tmem_slot - raw);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.x * kBM, n0 = blockIdx.y * kBN;
+    const int m0 = blockIdx.x * kRows, n0 = blockIdx.y * kBN;
     const int n_kb = (k_dim + kBK - 1) / kBK;
 
     if (threadIdx.x == 0) {
@@ -151,11 +160,15 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
             const uint32_t a_src = tiles + s * kStageBytes, b_src = a_src + kABytes;
 #pragma unroll
             for (int j = 0; j < kBK / kMmaK; ++j) {
-                const uint64_t da = smem_desc(a_src + j * kMmaK * 2), db = smem_desc(b_src + j * kMmaK * 2);
+                const uint64_t db = smem_desc(b_src + j * kMmaK * 2);
                 const uint32_t acc = (kb > 0 || j > 0) ? 1u : 0u;
-                asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                             " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
-                             ::"r"(tmem), "l"(da), "l"(db), "r"(kIdesc), "r"(acc) : "memory");
+#pragma unroll
+                for (int t = 0; t < kSub; ++t) {              // sub-tile t: W rows 128t.., TMEM columns 256t..
+                    const uint64_t da = smem_desc(a_src + t * kBM * 128 + j * kMmaK * 2);
+                    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n"
+                                 ::"r"(tmem + (uint32_t)(t * kBN)), "l"(da), "l"(db), "r"(kIdesc), "r"(acc) : "memory");
+                }
             }
             asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(empty(s)) : "memory");
         }
@@ -168,7 +181,8 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
     const bool acc_ok = __syncthreads_and(bar_wait(acc_bar, 0)) != 0;   // the same answer in every thread
     if (!acc_ok && threadIdx.x == 0) fail(status, 4);
     asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
-    const int row = warp * 32 + lane, m = m0 + row;
+    const int quarter = warp & 3, sub = warp >> 2;
+    const int row = quarter * 32 + lane, m = m0 + sub * kBM + row;   // row: TMEM lane, and row of a staged chunk
     const float gb = m < n_in ? gain * __half2float(bias[m]) : 0.f;
     __half *const urow = u + (int64_t)(m < n_in ? m : 0) * ldu;
     const bool staged = tma_out && acc_ok;                               // every MMA is done: the ring is free
@@ -177,7 +191,7 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
         const int n = n0 + c * kChunkCols;
         if (n >= batch) break;                                           // uniform over the CTA
         uint32_t r[32];
-        const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(c * 32);
+        const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)(sub * kBN + c * kChunkCols);
         asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15,"
                      " %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
                      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
@@ -189,7 +203,7 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
         if (staged) {
             // row `row` of chunk c: 64 bytes at c*8K + row*64, its 16-byte pieces in SWIZZLE_64B order
             // (piece q at q ^ ((row >> 1) & 3), the pattern the TMA store un-swizzles)
-            const uint32_t dst = tiles + c * kChunkBytes + row * 64;
+            const uint32_t dst = tiles + (sub * (kBN / kChunkCols) + c) * kChunkBytes + row * 64;
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
                 uint32_t h[4];
@@ -212,8 +226,9 @@ __global__ void __launch_bounds__(kThreads) input_map_kernel(const __grid_consta
         asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");  // the staged chunks, visible to TMA
         __syncthreads();
         if (threadIdx.x == 0) {
-            for (int c = 0; c < kBN / kChunkCols && n0 + c * kChunkCols < batch; ++c)
-                tma_store(&map_u, n0 + c * kChunkCols, m0, tiles + c * kChunkBytes);     // rows / columns past u: clipped
+            for (int t = 0; t < kSub && m0 + t * kBM < n_in; ++t)
+                for (int c = 0; c < kBN / kChunkCols && n0 + c * kChunkCols < batch; ++c)   // past u: clipped
+                    tma_store(&map_u, n0 + c * kChunkCols, m0 + t * kBM, tiles + (t * (kBN / kChunkCols) + c) * kChunkBytes);
             asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
             asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");         // smem read before the CTA exits
         }
@@ -281,7 +296,7 @@ extern "C" int afb_input_map_f16(int64_t n_in, int64_t batch, int64_t k_dim, con
         AFB_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
                   "W and x must be 16-byte aligned");
         CUtensorMap map_w, map_x, map_u;
-        encode_operand(&map_w, w, n_in, k_dim, ldw, kBM);
+        encode_operand(&map_w, w, n_in, k_dim, ldw, kRows);
         encode_operand(&map_x, x, batch, k_dim, ldx, kBN);
         const int tma_out = (ldu % 8 == 0 && (reinterpret_cast<uintptr_t>(u) & 15) == 0) ? 1 : 0;
         if (tma_out) encode_output(&map_u, u, n_in, batch, ldu);
@@ -293,7 +308,7 @@ extern "C" int afb_input_map_f16(int64_t n_in, int64_t batch, int64_t k_dim, con
             AFB_CUDA(cudaFuncSetAttribute(input_map_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes));
             configured[dev] = true;
         }
-        const dim3 grid((unsigned)((n_in + kBM - 1) / kBM), (unsigned)((batch + kBN - 1) / kBN));
+        const dim3 grid((unsigned)((n_in + kRows - 1) / kRows), (unsigned)((batch + kBN - 1) / kBN));
         AFB_CHECK(grid.y < 65536, "batch too large for one launch");
         input_map_kernel<<<grid, kThreads, kSmemBytes, (cudaStream_t)stream>>>(map_w, map_x, map_u, (int)n_in, (int)batch,
                                                                                (int)k_dim, static_cast<const __half *>(bias), gain,
