@@ -159,6 +159,10 @@ def input_map_f16(w16: torch.Tensor, b16: torch.Tensor, x: torch.Tensor, gain: f
     float16 with unit column stride; rows of x that do not start on 16 bytes are copied first.  The result
     is a view with a row stride rounded up to 8 positions (the light-cone forward reads it as it is)."""
     n_in, k = w16.shape
+    if not (w16.device == b16.device == x.device) or (status is not None and status.device != x.device):
+        raise RuntimeError("input_map_f16: w16, b16, x and status must be on one device")
+    if w16.dtype != torch.float16 or b16.dtype != torch.float16 or b16.shape != (n_in,):
+        raise ValueError("input_map_f16: w16 (n_in, k) and b16 (n_in,) must be float16")
     if w16.stride(1) != 1 or w16.stride(0) % 8 or w16.data_ptr() % 16:
         raise ValueError("w16 rows must be contiguous and start on 16-byte boundaries")
     if x.shape[1] != k:
@@ -171,10 +175,11 @@ def input_map_f16(w16: torch.Tensor, b16: torch.Tensor, x: torch.Tensor, gain: f
     ldu = -(-batch // 8) * 8
     u = torch.empty(n_in, ldu, dtype=torch.float16, device=x.device)[:, :batch]
     lib = _lib.load()
-    _lib.check(lib.afb_input_map_f16(n_in, batch, k, w16.data_ptr(), w16.stride(0), x.data_ptr(), x.stride(0),
-                                     b16.data_ptr(), float(gain), u.data_ptr(), ldu,
-                                     status.data_ptr() if status is not None else None,
-                                     torch.cuda.current_stream(x.device).cuda_stream))
+    with torch.cuda.device(x.device):                 # the launch goes to the device of the operands
+        _lib.check(lib.afb_input_map_f16(n_in, batch, k, w16.data_ptr(), w16.stride(0), x.data_ptr(), x.stride(0),
+                                         b16.data_ptr(), float(gain), u.data_ptr(), ldu,
+                                         status.data_ptr() if status is not None else None,
+                                         torch.cuda.current_stream(x.device).cuda_stream))
     return u
 
 

@@ -227,6 +227,25 @@ def test_input_map_kernel_against_float32(n_in, batch, k):
     assert int(status.item()) == 0
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_input_map_runs_on_the_operands_device():
+    """Called with cuda:1 operands while cuda:0 is current, the map runs on cuda:1 and equals cuda:0's."""
+    from alphafly_b200.model import input_map_f16
+    g = torch.Generator().manual_seed(9)
+    w = torch.randn(700, 838, generator=g) * 0.05
+    b = (torch.randn(700, generator=g) * 0.3).half()
+    bits = (torch.rand(300, 838, generator=g) < 0.06).half()
+    outs = []
+    for dev in ("cuda:0", "cuda:1"):
+        w16 = torch.zeros(700, 840, dtype=torch.float16, device=dev)[:, :838]
+        w16.copy_(w)
+        st = torch.zeros(1, dtype=torch.int32, device=dev)
+        with torch.cuda.device(0):
+            outs.append(input_map_f16(w16, b.to(dev), bits.to(dev), 5.0, st).cpu())
+        assert int(st.item()) == 0
+    assert torch.equal(outs[0], outs[1])
+
+
 def test_web_model_round_trip_evaluates_like_the_exported_network(small_net, tmp_path):
     """export_web_model -> net_from_web_model on configuration 1's network: the manifest's test vectors
     (float32 logits of legal moves and values, made on the original network) are reproduced by the rebuilt
