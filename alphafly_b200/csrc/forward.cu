@@ -274,6 +274,7 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
             a.ts_out = (int64_t)sp.n_rows * bt;
             a.batch = batch;
             a.err = c->err.get();
+            a.post = mode == AFB_MODE_DEV16 ? sp.op.post.get() : nullptr;
             if (events) AFB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[t - 1]), s));
             if (mode == AFB_MODE_F32) launch_step_f32(a, s);
             else launch_step_dev16(a, s);

@@ -103,6 +103,7 @@ struct StepArgs {
     int64_t batch;
     int *err;                      // device status word: set non-zero when a bounded wait gives up
     float *y_out;                  // training forward: pre-clamp drive of R_t, tile-major (float32 state only)
+    const int *post;               // local row of each synapse (float16 forward: enables the tensor-core step)
 };
 
 // Batch columns one CTA covers for a state element of `elem_bytes`; the state's leading dimension is
@@ -114,6 +115,9 @@ inline int64_t padded_ld(int64_t batch, int elem_bytes) {
 }
 
 void launch_step_f32(const StepArgs &a, cudaStream_t s);
+// the tensor-core step for short rows (step_tc.cu): float16 deviation state, dense tile-major output
+bool step_tc_eligible(const StepArgs &a);
+void launch_step_tc(const StepArgs &a, cudaStream_t s);
 void launch_step_dev16(const StepArgs &a, cudaStream_t s);
 
 // out[o, b] = src[o] >= 0 ? (add_base ? base[o] : 0) + state[src[o], b] : base[o]   (float32 out, row-major);

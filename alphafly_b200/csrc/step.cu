@@ -23,6 +23,8 @@
 // shared-memory ring with cp.async, which keeps more bytes in flight but moves every row through the
 // L1 data pipe three times; on B200 it reaches 10 TB/s (its own ceiling), the register kernel 12 TB/s.
 // Accumulation is float32 in every mode.
+#include <cstdlib>
+
 #include "internal.cuh"
 
 namespace afb {
@@ -732,6 +734,13 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
     }
 }
 
+bool step_tc_enabled() {
+    static const bool on = [] {
+        const char *v = std::getenv("AFB_STEP_TC");
+        return v && v[0] == '1';
+    }();
+    return on;
+}
 #ifndef AFB_RING_MAX_DEGREE
 #define AFB_RING_MAX_DEGREE 16
 #endif
@@ -765,6 +774,15 @@ void launch(const StepArgs &args, cudaStream_t s) {
     }
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
+    // Float16 sub-matrices with short rows on the tensor cores (step_tc.cu), when switched on: measured
+    // slower than the ring kernel on configuration 3's step 2, so off unless AFB_STEP_TC=1 is set in the
+    // environment (read once per process).
+    if constexpr (sizeof(T) == 2) {
+        if (step_tc_enabled() && !AFB_RING && a.nnz < kRingMaxDegree * (int64_t)a.n_rows && step_tc_eligible(a)) {
+            launch_step_tc(a, s);
+            return;
+        }
+    }
     // The ring kernel keeps gathers in flight across row ends, which pays on sub-matrices whose rows are
     // shorter than half a 32-synapse window (configuration 3's steps 1 and 2: 0.85 vs 1.04 ms on step 1,
     // which has no synapses, equal on step 2); the register kernel wins on the others.  Both give bitwise
