@@ -734,6 +734,8 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
     }
 }
 
+// Whether float16 short-row steps take the tensor-core kernel of step_tc.cu: AFB_STEP_TC=1 in the
+// environment, read on the first launch of the process.
 bool step_tc_enabled() {
     static const bool on = [] {
         const char *v = std::getenv("AFB_STEP_TC");
