@@ -12,6 +12,7 @@ import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libafb.so")
+PROBE_PATH = os.path.join(_HERE, "libafb_probe.so")      # bench.py's gather-ceiling probe (include/afb_probe.h)
 
 OK, EINVAL, ECUDA, ESTATE = 0, -1, -2, -3
 MODE_F32, MODE_DEV16 = 0, 1
@@ -26,7 +27,7 @@ _f = ctypes.c_float
 _sz = ctypes.c_size_t
 _pp = ctypes.POINTER(ctypes.c_void_p)
 
-# name -> (restype, argtypes); every entry point of include/afb.h and include/afb_probe.h
+# name -> (restype, argtypes); every entry point of include/afb.h
 SIGNATURES = {
     "afb_last_error": (ctypes.c_char_p, []),
     "afb_version": (_int, []),
@@ -54,11 +55,16 @@ SIGNATURES = {
     "afb_graph_forward": (_int, [_p, _p, _p, _p, _f, _p, _i64, _i64, _int, _p, _i64, _p, _sz, _p]),
     "afb_legal_logits": (_int, [_i64, _p, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "afb_input_map_f16": (_int, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _f, _p, _i64, _p, _p]),
+}
+
+# the entry points of include/afb_probe.h (libafb_probe.so)
+PROBE_SIGNATURES = {
     "afb_probe_gather_sink_words": (_i64, []),
-    "afb_probe_gather": (_int, [_int, _int, _p, _i64, _p, _i64, _p, _i64, _p]),
+    "afb_probe_gather": (_int, [_int, _p, _i64, _p, _i64, _p, _i64, _p]),
 }
 
 _lib = None
+_probe = None
 
 
 def load() -> ctypes.CDLL:
@@ -75,6 +81,21 @@ def load() -> ctypes.CDLL:
             fn.argtypes = args
         _lib = lib
     return _lib
+
+
+def load_probe() -> ctypes.CDLL:
+    """bench.py's gather-ceiling probe library (built beside libafb.so by the same Makefile)."""
+    global _probe
+    if _probe is None:
+        if not os.path.exists(PROBE_PATH):
+            raise ImportError(f"{PROBE_PATH} is missing: build it with `make -C {os.path.join(_HERE, 'csrc')}`")
+        lib = ctypes.CDLL(PROBE_PATH)
+        for name, (res, args) in PROBE_SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _probe = lib
+    return _probe
 
 
 class AfbError(RuntimeError):

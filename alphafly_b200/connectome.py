@@ -55,11 +55,6 @@ class Connectome:
         neuron_sign = torch.ones(self.n_neurons).index_put_((self.pre,), self.sign)
         return Connectome(self.neurons, pre[order], self.post[order], self.syn_count[order], neuron_sign[pre[order]])
 
-    def summary(self) -> str:
-        flows = self.neurons["flow"].value_counts().to_dict()
-        return (f"{self.n_neurons:,} neurons, {self.n_edges:,} edges, "
-                f"{float((self.sign > 0).float().mean()):.1%} excitatory, flow={flows}")
-
 
 def neuron_table(n: int, afferent: np.ndarray, efferent: np.ndarray) -> pd.DataFrame:
     """A neuron table with the given afferent (input) and efferent (output) neurons; the rest intrinsic."""

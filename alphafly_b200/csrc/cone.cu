@@ -246,6 +246,7 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
         c->n = n;
         c->e = e;
         c->steps = steps;
+        AFB_CUDA(cudaGetDevice(&c->device));
         c->n_in = n_in;
         c->n_out = n_out;
         Temp tmp;

@@ -274,7 +274,6 @@ int afb_cone_forward_timed(const afb_cone *c, int mode, const void *u_in, int64_
             a.ts_out = (int64_t)sp.n_rows * bt;
             a.batch = batch;
             a.err = c->err.get();
-            a.post = mode == AFB_MODE_DEV16 ? sp.op.post.get() : nullptr;
             if (events) AFB_CUDA(cudaEventRecord(static_cast<cudaEvent_t>(events[t - 1]), s));
             if (mode == AFB_MODE_F32) launch_step_f32(a, s);
             else launch_step_dev16(a, s);
@@ -370,14 +369,12 @@ int afb_graph_forward(const afb_graph *g, const float *w, const float *bias, con
 static __device__ __align__(256) unsigned char g_noalloc_scratch[AFB_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-// Device address of g_noalloc_scratch on the current device.  In host code the symbol's name is a
-// host-side stand-in, not a device address, so it is resolved once per device with cudaGetSymbolAddress
-// (with that device current) and cached.
-void *noalloc_scratch() {
+// Device address of g_noalloc_scratch on device `dev`, which must be current.  In host code the symbol's
+// name is a host-side stand-in, not a device address, so it is resolved once per device with
+// cudaGetSymbolAddress (with that device current) and cached for the life of the process.
+void *noalloc_scratch(int dev) {
     static std::mutex lock;
     static void *addr[64] = {};
-    int dev = 0;
-    AFB_CUDA(cudaGetDevice(&dev));
     AFB_CHECK(dev >= 0 && dev < 64, "device index out of range for the built-in scratch");
     std::lock_guard<std::mutex> g(lock);
     if (!addr[dev]) {
@@ -401,7 +398,19 @@ int afb_cone_forward_noalloc(const afb_cone *c, int mode, const void *u_in, int6
                   "afb_cone_forward_noalloc: this cone and batch need " + std::to_string(need) +
                       " bytes of state, more than the built-in scratch of " + std::to_string(AFB_NOALLOC_SCRATCH_BYTES) +
                       " bytes; use afb_cone_forward with a caller-provided workspace or a smaller batch");
-        ws = noalloc_scratch();
+        // The scratch is picked by device, so the device must be the cone's, and the stream's: a mismatch
+        // would run this cone's kernels against another GPU's array.
+        int dev = -1;
+        AFB_CUDA(cudaGetDevice(&dev));
+        AFB_CHECK(dev == c->device, "afb_cone_forward_noalloc: the current device (" + std::to_string(dev) +
+                                        ") is not the cone's device (" + std::to_string(c->device) + ")");
+        if (stream) {
+            int sdev = -1;
+            AFB_CUDA(cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev));
+            AFB_CHECK(sdev == c->device, "afb_cone_forward_noalloc: the stream belongs to device " + std::to_string(sdev) +
+                                             ", not the cone's device (" + std::to_string(c->device) + ")");
+        }
+        ws = noalloc_scratch(dev);
     });
     if (rc != AFB_OK) return rc;
     return afb_cone_forward_timed(c, mode, u_in, ld_u, batch, out, ld_out, ws, AFB_NOALLOC_SCRATCH_BYTES, nullptr, stream);

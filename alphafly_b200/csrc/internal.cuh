@@ -60,18 +60,11 @@ struct Step {
     DevBuf<__half> val16;          // half(w[edges]), AFB_MODE_DEV16
 };
 
-// Compile-time tuning of the step kernel (defaults are the shipped configuration).
-#ifndef AFB_ITEM_COST
-#define AFB_ITEM_COST 4096
-#endif
-
-// Schedule target: cost units (edges + kRowCost per row) per CTA work item.
+// Schedule target: cost units (edges + kRowCost per row) per CTA work item, and the finer target of
+// launches whose kItemCost items would be too few CTAs to fill the GPU.
 constexpr int kRowCost = 4;
-constexpr int kItemCost = AFB_ITEM_COST;
-#ifndef AFB_FINE_ITEM_COST
-#define AFB_FINE_ITEM_COST 512
-#endif
-constexpr int kFineItemCost = AFB_FINE_ITEM_COST;
+constexpr int kItemCost = 4096;
+constexpr int kFineItemCost = 512;
 
 // Builds the item schedule of `m` from its crow (device), then its merge-path table; synchronous.
 void build_schedule(Csr &m, cudaStream_t s);
@@ -103,7 +96,6 @@ struct StepArgs {
     int64_t batch;
     int *err;                      // device status word: set non-zero when a bounded wait gives up
     float *y_out;                  // training forward: pre-clamp drive of R_t, tile-major (float32 state only)
-    const int *post;               // local row of each synapse (float16 forward: enables the tensor-core step)
 };
 
 // Batch columns one CTA covers for a state element of `elem_bytes`; the state's leading dimension is
@@ -115,9 +107,6 @@ inline int64_t padded_ld(int64_t batch, int elem_bytes) {
 }
 
 void launch_step_f32(const StepArgs &a, cudaStream_t s);
-// the tensor-core step for short rows (step_tc.cu): float16 deviation state, dense tile-major output
-bool step_tc_eligible(const StepArgs &a);
-void launch_step_tc(const StepArgs &a, cudaStream_t s);
 void launch_step_dev16(const StepArgs &a, cudaStream_t s);
 
 // out[o, b] = src[o] >= 0 ? (add_base ? base[o] : 0) + state[src[o], b] : base[o]   (float32 out, row-major);
@@ -138,6 +127,7 @@ void launch_spmv(int n_rows, const int *crow, const int *col, const float *val, 
 struct afb_cone {
     int64_t n = 0, e = 0;
     int steps = 0;
+    int device = -1;                  // the CUDA device that was current at creation: the cone's buffers live there
     std::vector<afb::Step> st;        // st[0..steps]; st[0] holds R_0 only
     afb::DevBuf<int> full_crow, full_col, full_post;   // W in CSR (edge order) with each edge's row
     afb::DevBuf<int> full_tcrow, full_tcol, full_torder; // W^T in CSR and the edge permutation into it

@@ -19,12 +19,11 @@
 // The cost is the gather: every synapse pulls one 512-byte row of the previous state from L2.  Two
 // kernels implement it.  The default (step_kernel) loads kChunk gathered rows per lane straight into
 // registers; its throughput is set by the loads in flight per SM, so it is written to fit 48 registers
-// (5 CTAs, 40 warps per SM).  The alternative (AFB_RING=1, step_kernel_ring) stages the rows in a
-// shared-memory ring with cp.async, which keeps more bytes in flight but moves every row through the
-// L1 data pipe three times; on B200 it reaches 10 TB/s (its own ceiling), the register kernel 12 TB/s.
+// (5 CTAs, 40 warps per SM).  The other (step_kernel_ring) stages the rows in a shared-memory ring with
+// cp.async, which keeps gathers in flight across row ends but moves every row through the L1 data pipe
+// three times; on B200 it reaches 10 TB/s (its own ceiling), the register kernel 12 TB/s.  The ring
+// kernel runs the sub-matrices whose rows are short (see launch).
 // Accumulation is float32 in every mode.
-#include <cstdlib>
-
 #include "internal.cuh"
 
 namespace afb {
@@ -78,19 +77,6 @@ struct Lane<__half> {
 // p = previous state (or the constant pc), out = p + a (x - p); written to the tile-major x_out (and
 // y to y_out in the training forward).  The previous state and the drive are kept packed and converted
 // a pair at a time, to keep few registers live.
-// One-pass traffic (sub-matrix indices and values, the input drive, the new state) can be marked
-// streaming (ld/st .cs: evict first), leaving L2 to the gathered slab.
-#ifndef AFB_STREAM_CS
-#define AFB_STREAM_CS 0
-#endif
-template <typename X>
-__device__ __forceinline__ X ld_once(const X *p) { return AFB_STREAM_CS ? __ldcs(p) : __ldg(p); }
-template <typename X>
-__device__ __forceinline__ void st_once(X *p, const X &v) {
-    if (AFB_STREAM_CS) __stcs(p, v);
-    else *p = v;
-}
-
 template <typename T, int BT>
 __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t tile, int off, const float (&acc)[Lane<T>::V]) {
     constexpr int V = Lane<T>::V;
@@ -101,7 +87,7 @@ __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t t
     uint4 up = make_uint4(0, 0, 0, 0), pp = make_uint4(0, 0, 0, 0);
     const T *u = static_cast<const T *>(a.u) + (int64_t)(usrc >= 0 ? usrc : 0) * a.ld_u + col0;
     const bool u_vec = usrc >= 0 && a.u_vec_ok && col0 + V <= a.batch;
-    if (u_vec) up = ld_once(reinterpret_cast<const uint4 *>(u));
+    if (u_vec) up = __ldg(reinterpret_cast<const uint4 *>(u));
     if (prev >= 0) pp = __ldg(reinterpret_cast<const uint4 *>(static_cast<const T *>(a.x_in) + tile * a.ts_in + (int64_t)prev * BT + off));
     const float kk = __int_as_float(w0.x), lo = __int_as_float(w0.y), hi = __int_as_float(w0.z), e = __int_as_float(w0.w);
     const float pc = __int_as_float(w1.x), al = __int_as_float(w1.y);
@@ -137,11 +123,11 @@ __device__ __forceinline__ void finish_row(const StepArgs &a, int row, int64_t t
             yr[k] = __float_as_uint(y[0]);
         }
     }
-    st_once(reinterpret_cast<uint4 *>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off),
-            make_uint4(outr[0], outr[1], outr[2], outr[3]));
+    *reinterpret_cast<uint4 *>(static_cast<T *>(a.x_out) + tile * a.ts_out + (int64_t)row * BT + off) =
+        make_uint4(outr[0], outr[1], outr[2], outr[3]);
     if constexpr (sizeof(T) == 4)
         if (a.y_out)
-            st_once(reinterpret_cast<uint4 *>(a.y_out + tile * a.ts_out + (int64_t)row * BT + off), make_uint4(yr[0], yr[1], yr[2], yr[3]));
+            *reinterpret_cast<uint4 *>(a.y_out + tile * a.ts_out + (int64_t)row * BT + off) = make_uint4(yr[0], yr[1], yr[2], yr[3]);
 }
 
 __global__ void output_kernel(int n_out, const int *__restrict__ src, const float *__restrict__ base, int add_base,
@@ -185,37 +171,17 @@ __global__ void spmv_kernel(int n_rows, const int *__restrict__ crow, const int 
 // float32, so the mixed-precision fma.rn.f32.f16 (float16 inputs, float32 accumulator, one rounding)
 // gives the same sums as converting first, at half the instructions; float32 state uses the packed
 // fma.rn.f32x2.  Row constants of the warp's next 32 rows are staged in shared memory.
-#ifndef AFB_RING_STAGES
-#define AFB_RING_STAGES 3
-#endif
-#ifndef AFB_RING_CHUNK
-#define AFB_RING_CHUNK 4
-#endif
-#ifndef AFB_RING_MINBLOCKS
-#define AFB_RING_MINBLOCKS 3
-#endif
-constexpr int kStages = AFB_RING_STAGES;
-constexpr int kChunk = AFB_RING_CHUNK;
+constexpr int kStages = 3;      // tuned on configuration 3's step 2: 3 stages of 4 synapses, 3 CTAs per SM
+constexpr int kChunk = 4;
+constexpr int kRingMinBlocks = 3;
 constexpr int kWarpRing = kStages * kChunk * kRowBytes;
 constexpr int kRingBytes = kWarps * kWarpRing;
 static_assert(32 % kChunk == 0, "a chunk must not straddle a 32-edge window");
 static_assert(kWarpRing >= 256 * 4, "a warp's ring must hold its cut-row partial after the main loop");
 
-#ifndef AFB_CP_CG
-#define AFB_CP_CG 0
-#endif
-// Through L1 (.ca) a warp's 32 x 16 contiguous bytes coalesce into four 128-byte requests; the L2-only
-// form (.cg) was measured to move twice the gathered bytes from L2.
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
-    if (AFB_CP_CG) asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-    else asm volatile("cp.async.ca.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
-}
-// L2 eviction priorities: the gathered slab of a tile is read ~60 times while the tile is processed,
-// everything else (sub-matrix indices and values, the input drive, the new state) once.  Marking the
-// one-pass traffic evict-first and the slab evict-last keeps the slab resident in L2.
-#ifndef AFB_L2HINT
-#define AFB_L2HINT 1
-#endif
+// L2 eviction priorities of the ring kernel: the gathered slab of a tile is read ~60 times while the tile
+// is processed, everything else (sub-matrix indices and values, the input drive, the new state) once.
+// Marking the one-pass traffic evict-first and the slab evict-last keeps the slab resident in L2.
 __device__ __forceinline__ uint64_t policy_keep() {
     uint64_t p;
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;\n" : "=l"(p));
@@ -226,47 +192,35 @@ __device__ __forceinline__ uint64_t policy_stream() {
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(p));
     return p;
 }
+// Through L1 (.ca) a warp's 32 x 16 contiguous bytes coalesce into four 128-byte requests; the L2-only
+// form (.cg) was measured to move twice the gathered bytes from L2.
 __device__ __forceinline__ void cp_async16_hint(uint32_t dst, const void *src, uint64_t pol) {
-    if (!AFB_L2HINT) return cp_async16(dst, src);
     asm volatile("cp.async.ca.shared.global.L2::cache_hint [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "l"(pol) : "memory");
 }
 __device__ __forceinline__ uint32_t ld_stream_b32(const void *p, uint64_t pol) {
     uint32_t v;
-    if (AFB_L2HINT) asm volatile("ld.global.nc.L2::cache_hint.b32 %0, [%1], %2;\n" : "=r"(v) : "l"(p), "l"(pol));
-    else v = __ldg(static_cast<const unsigned *>(p));
+    asm volatile("ld.global.nc.L2::cache_hint.b32 %0, [%1], %2;\n" : "=r"(v) : "l"(p), "l"(pol));
     return v;
 }
 __device__ __forceinline__ uint32_t ld_stream_b16(const void *p, uint64_t pol) {
     unsigned short v;
-    if (AFB_L2HINT) asm volatile("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;\n" : "=h"(v) : "l"(p), "l"(pol));
-    else v = __ldg(static_cast<const unsigned short *>(p));
+    asm volatile("ld.global.nc.L2::cache_hint.b16 %0, [%1], %2;\n" : "=h"(v) : "l"(p), "l"(pol));
     return v;
 }
 __device__ __forceinline__ uint4 ld_stream_v4(const void *p, uint64_t pol) {
     uint4 v;
-    if (AFB_L2HINT)
-        asm volatile("ld.global.nc.L2::cache_hint.v4.b32 {%0, %1, %2, %3}, [%4], %5;\n"
-                     : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p), "l"(pol));
-    else v = __ldg(static_cast<const uint4 *>(p));
+    asm volatile("ld.global.nc.L2::cache_hint.v4.b32 {%0, %1, %2, %3}, [%4], %5;\n"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p), "l"(pol));
     return v;
 }
 __device__ __forceinline__ void st_stream_v4(void *p, uint4 v, uint64_t pol) {
-    if (AFB_L2HINT)
-        asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;\n" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
-                     "r"(v.w), "l"(pol) : "memory");
-    else *static_cast<uint4 *>(p) = v;
+    asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1, %2, %3, %4}, %5;\n" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w), "l"(pol) : "memory");
 }
 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory"); }
-
-// How a float16 row slice is multiplied into the float32 accumulators: 0 = mixed-precision
-// fma.rn.f32.f16, 1 = convert half2 -> float2 then fmaf, 2 = convert then packed fma.rn.f32x2.
-// All three round each product-sum once in float32 and give the same results.
-#ifndef AFB_HALF_MATH
-#define AFB_HALF_MATH 0
-#endif
 
 template <typename T>
 struct Gather;
@@ -275,17 +229,18 @@ template <>
 struct Gather<__half> {
     static constexpr int V = 8;
     __device__ static uint32_t bits(const __half *p, uint64_t pol) { return ld_stream_b16(p, pol); }
-    __device__ static uint32_t bits_plain(const __half *p) { return ld_once(reinterpret_cast<const unsigned short *>(p)); }
+    __device__ static uint32_t bits_plain(const __half *p) { return __ldg(reinterpret_cast<const unsigned short *>(p)); }
     // acc[0..7] += v * x[0..7], x = the 8 float16 values at shared address addr
     __device__ static void fma(float (&acc)[8], uint32_t v, uint32_t addr) {
         uint4 x;
         asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w) : "r"(addr));
         fma(acc, v, x);
     }
-    // acc[0..7] += v * x[0..7], x = 8 float16 values in registers
+    // acc[0..7] += v * x[0..7], x = 8 float16 values in registers.  The mixed-precision fma.rn.f32.f16
+    // multiplies two float16 values exactly in float32 and rounds the sum once, so it equals converting
+    // first, at half the instructions.
     __device__ static void fma(float (&acc)[8], uint32_t v, const uint4 &x) {
         const uint32_t r[4] = {x.x, x.y, x.z, x.w};
-#if AFB_HALF_MATH == 0
         const unsigned short vh = (unsigned short)v;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -294,21 +249,6 @@ struct Gather<__half> {
             asm("fma.rn.f32.f16 %0, %1, %2, %0;\n" : "+f"(acc[2 * k]) : "h"(lo), "h"(vh));
             asm("fma.rn.f32.f16 %0, %1, %2, %0;\n" : "+f"(acc[2 * k + 1]) : "h"(hi), "h"(vh));
         }
-#else
-        const float vf = __half2float(__ushort_as_half((unsigned short)v));
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&r[k]));
-#if AFB_HALF_MATH == 1
-            acc[2 * k] = fmaf(vf, f.x, acc[2 * k]);
-            acc[2 * k + 1] = fmaf(vf, f.y, acc[2 * k + 1]);
-#else
-            asm("{\n .reg .b64 a, x, v;\n mov.b64 a, {%0, %1};\n mov.b64 x, {%2, %3};\n mov.b64 v, {%4, %4};\n"
-                " fma.rn.f32x2 a, x, v, a;\n mov.b64 {%0, %1}, a;\n}\n"
-                : "+f"(acc[2 * k]), "+f"(acc[2 * k + 1]) : "f"(f.x), "f"(f.y), "f"(vf));
-#endif
-        }
-#endif
     }
 };
 
@@ -316,7 +256,7 @@ template <>
 struct Gather<float> {
     static constexpr int V = 4;
     __device__ static uint32_t bits(const float *p, uint64_t pol) { return ld_stream_b32(p, pol); }
-    __device__ static uint32_t bits_plain(const float *p) { return ld_once(reinterpret_cast<const unsigned *>(p)); }
+    __device__ static uint32_t bits_plain(const float *p) { return __ldg(reinterpret_cast<const unsigned *>(p)); }
     __device__ static void fma(float (&acc)[4], uint32_t v, uint32_t addr) {
         uint4 x;
         asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];\n" : "=r"(x.x), "=r"(x.y), "=r"(x.z), "=r"(x.w) : "r"(addr));
@@ -416,7 +356,7 @@ __device__ __forceinline__ void finish_row_pre(const StepArgs &a, const RowConst
 }
 
 template <typename T, typename TV>
-__global__ void __launch_bounds__(kWarps * 32, AFB_RING_MINBLOCKS) step_kernel_ring(const StepArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, kRingMinBlocks) step_kernel_ring(const StepArgs a) {
     using G = Gather<T>;
     constexpr int V = G::V;
     constexpr int BT = 32 * V;
@@ -595,19 +535,8 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_RING_MINBLOCKS) step_kernel_r
 // the configuration-3 workload: the gather's throughput grows with the warps per SM, and a spill in the
 // loop costs more than any occupancy gains, so the tuned point is kChunk = 4 at 5 CTAs per SM (48
 // registers, no spills).
-#ifndef AFB_RING
-#define AFB_RING 0
-#endif
-#ifndef AFB_CHUNK
-#define AFB_CHUNK 4
-#endif
-#ifndef AFB_MINBLOCKS
-#define AFB_MINBLOCKS 5
-#endif
-#ifndef AFB_FULL_WINDOW
-#define AFB_FULL_WINDOW 1    // unpredicated path for the full chunks of a window
-#endif
-constexpr int kChunkR = AFB_CHUNK;
+constexpr int kChunkR = 4;      // gathered rows in flight per lane
+constexpr int kMinBlocks = 5;   // CTAs per SM: 40 warps at 48 registers per thread
 
 // Per-warp loop bounds live in shared memory and are re-read where they are needed (volatile), so
 // that they do not hold registers through the gather loop.
@@ -617,7 +546,7 @@ struct LeanWarp {
 __device__ __forceinline__ int vld(const int &x) { return *reinterpret_cast<const volatile int *>(&x); }
 
 template <typename T, typename TV>
-__global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(kWarps * 32, kMinBlocks) step_kernel(const StepArgs a) {
     using G = Gather<T>;
     constexpr int V = G::V;
     constexpr int BT = 32 * V;
@@ -678,11 +607,11 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
             int my_col = 0;
             uint32_t my_val = 0u;
             if (lane < n) {
-                my_col = ld_once(a.col + eoff);
+                my_col = __ldg(a.col + eoff);
                 my_val = G::bits_plain(static_cast<const TV *>(a.val) + eoff);
             }
             // full chunks: nothing predicated (chunks kept in sequence: one chunk's rows in registers at a time)
-            const int n_full = AFB_FULL_WINDOW ? n / kChunkR * kChunkR : 0;
+            const int n_full = n / kChunkR * kChunkR;
 #pragma unroll 1
             for (int k = 0; k < n_full; k += kChunkR) {
                 uint4 x[kChunkR];
@@ -734,19 +663,8 @@ __global__ void __launch_bounds__(kWarps * 32, AFB_MINBLOCKS) step_kernel(const 
     }
 }
 
-// Whether float16 short-row steps take the tensor-core kernel of step_tc.cu: AFB_STEP_TC=1 in the
-// environment, read on the first launch of the process.
-bool step_tc_enabled() {
-    static const bool on = [] {
-        const char *v = std::getenv("AFB_STEP_TC");
-        return v && v[0] == '1';
-    }();
-    return on;
-}
-#ifndef AFB_RING_MAX_DEGREE
-#define AFB_RING_MAX_DEGREE 16
-#endif
-constexpr int64_t kRingMaxDegree = AFB_RING_MAX_DEGREE;  // sub-matrices with shorter mean rows take the ring kernel
+// Sub-matrices whose mean row is shorter than this take the ring kernel.
+constexpr int64_t kRingMaxDegree = 16;
 
 // CTAs below which a step takes the fine schedule: two waves of the register kernel's 5 CTAs per SM.
 int64_t fine_grid_limit() {
@@ -755,7 +673,7 @@ int64_t fine_grid_limit() {
     AFB_CUDA(cudaGetDevice(&dev));
     if (dev >= 64) return 0;
     if (!sms[dev]) AFB_CUDA(cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev));
-    return 2LL * AFB_MINBLOCKS * sms[dev];
+    return 2LL * kMinBlocks * sms[dev];
 }
 
 template <typename T, typename TV>
@@ -776,20 +694,11 @@ void launch(const StepArgs &args, cudaStream_t s) {
     }
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
-    // Float16 sub-matrices with short rows on the tensor cores (step_tc.cu), when switched on: measured
-    // slower than the ring kernel on configuration 3's step 2, so off unless AFB_STEP_TC=1 is set in the
-    // environment (read once per process).
-    if constexpr (sizeof(T) == 2) {
-        if (step_tc_enabled() && !AFB_RING && a.nnz < kRingMaxDegree * (int64_t)a.n_rows && step_tc_eligible(a)) {
-            launch_step_tc(a, s);
-            return;
-        }
-    }
     // The ring kernel keeps gathers in flight across row ends, which pays on sub-matrices whose rows are
     // shorter than half a 32-synapse window (configuration 3's steps 1 and 2: 0.85 vs 1.04 ms on step 1,
     // which has no synapses, equal on step 2); the register kernel wins on the others.  Both give bitwise
     // the same results.
-    const bool ring = AFB_RING || a.nnz < kRingMaxDegree * (int64_t)a.n_rows;
+    const bool ring = a.nnz < kRingMaxDegree * (int64_t)a.n_rows;
     if (ring) {
         static unsigned long long configured = 0;   // devices on which this instantiation may use kRingBytes
         int dev = 0;

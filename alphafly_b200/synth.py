@@ -204,4 +204,13 @@ def drive(inst: Instance, batch: int, seed: int = 0, input_gain: float = 5.0) ->
     return np.ascontiguousarray((enc * input_gain).T.astype(np.float32))
 
 
+def config3_drive(inst: Instance, batch: int, rank: int = 0, block: int = 2048) -> np.ndarray:
+    """The benchmark's float16 drive of configuration 3 for ``rank``: ``block`` distinct positions
+    (``drive`` with seed 1000 + rank) repeated to ``batch`` columns, (I, batch) float16.  The step kernel's
+    gathers do not depend on the values, so the repetition changes no work; column c is position c % block."""
+    base = drive(inst, min(batch, block), seed=1000 + rank).astype(np.float16)
+    reps = -(-batch // base.shape[1])
+    return np.ascontiguousarray(np.tile(base, (1, reps))[:, :batch])
+
+
 CONFIGS = {"small": small, "full": full, "shuffled": shuffled}

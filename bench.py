@@ -14,7 +14,7 @@ the drive in pinned host memory and the output copied back inside the timed regi
 ``--impl reference`` times the reference algorithm's CPU implementation (the float32 port in
 oracle/, all host threads) on a bounded sample of the same workload and prints the same line.
 ``--train`` times configuration 5 instead (FlyChessNet train_step, B = 2,048 per GPU, data parallel over
-NCCL under torchrun); ``--probe`` prints the device's gather ceiling for each load path; ``--evaluator``
+NCCL under torchrun); ``--probe`` prints the device's gather ceiling against warps per SM; ``--evaluator``
 times self-play evaluation rounds (B = 1,120 positions) through three implementations of the Evaluator.
 """
 
@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--train", action="store_true",
                     help="time the training step instead (configuration 5: FlyChessNet train_step, B = 2,048 per GPU)")
-    ap.add_argument("--probe", action="store_true", help="print the gather ceiling of every load path and exit")
+    ap.add_argument("--probe", action="store_true", help="print the gather ceiling of the step kernel's load path and exit")
     ap.add_argument("--configs", action="store_true",
                     help="time configurations 1, 2 and 4 (the other workloads of the scope; one JSON line each)")
     ap.add_argument("--evaluator", action="store_true",
@@ -96,30 +96,34 @@ def measured_traffic():
     return None
 
 
-def gather_ceiling(dev, slab_rows, n_rows=1 << 25, reps=5, path=0, blocks_per_sm=0):
+def gather_ceiling(dev, slab_rows, n_rows=1 << 25, reps=5, blocks_per_sm=0):
     """Device ceiling of the step kernel's dominant access: n_rows random 512-byte rows of a slab of
-    ``slab_rows`` rows gathered by the library's probe kernel through load path ``path`` (include/afb_probe.h;
-    0 = 16-byte loads into registers); GB/s (median of reps)."""
+    ``slab_rows`` rows gathered by the probe kernel of libafb_probe.so (include/afb_probe.h: 16-byte loads into
+    registers, 8 rows in flight per lane, ``blocks_per_sm`` CTAs of 8 warps per SM, 0 = 8); GB/s (median of
+    reps)."""
     from alphafly_b200 import _lib
-    lib = _lib.load()
+    lib = _lib.load_probe()
     g = torch.Generator(device=dev).manual_seed(5)
-    narrow = path in (7, 8)                       # 256-byte rows: each slab row counts as two
     slab = torch.randint(0, 1 << 30, (slab_rows, 128), dtype=torch.int32, device=dev, generator=g)
-    rows = torch.randint(0, slab_rows * (2 if narrow else 1), (n_rows,), dtype=torch.int32, device=dev, generator=g)
+    rows = torch.randint(0, slab_rows, (n_rows,), dtype=torch.int32, device=dev, generator=g)
     words = lib.afb_probe_gather_sink_words()
+    if words < 0:
+        raise RuntimeError("afb_probe_gather_sink_words failed")
     sink = torch.empty(words, dtype=torch.int32, device=dev)
     stream = torch.cuda.current_stream(dev)
-    args = (path, blocks_per_sm, slab.data_ptr(), slab_rows, rows.data_ptr(), n_rows, sink.data_ptr(), words, stream.cuda_stream)
+    args = (blocks_per_sm, slab.data_ptr(), slab_rows, rows.data_ptr(), n_rows, sink.data_ptr(), words, stream.cuda_stream)
     times = []
     for k in range(3 + reps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(stream)
-        _lib.check(lib.afb_probe_gather(*args))
+        rc = lib.afb_probe_gather(*args)
+        if rc != 0:
+            raise RuntimeError(f"afb_probe_gather failed with code {rc}")
         b.record(stream)
         b.synchronize()
         if k >= 3:
             times.append(a.elapsed_time(b))
-    return n_rows * (256 if narrow else 512) / (statistics.median(times) / 1000.0) / 1e9
+    return n_rows * 512 / (statistics.median(times) / 1000.0) / 1e9
 
 
 def workload(seed=0):
@@ -257,26 +261,13 @@ def reference_arm(args, rank, world):
 
 
 def probe_arm(args):
-    """Gather ceiling of each load path of include/afb_probe.h on configuration 3's widest slab, and of the
-    register path against warps per SM."""
+    """Gather ceiling of the step kernel's load path (include/afb_probe.h) on configuration 3's widest slab,
+    against warps per SM."""
     dev = torch.device("cuda", 0)
     rows = 166_688
-    names = {0: "ldg x8", 1: "cp.async", 2: "cp.async + read-back", 3: "tma gather4", 4: "tma gather4 + read-back",
-             5: "ldg x4", 6: "ldg x16"}
-    for path in (0, 1, 2, 3, 4):
-        print(json.dumps({"probe": names[path], "slab_rows": rows, "gbs": round(gather_ceiling(dev, rows, path=path), 1)}),
-              flush=True)
-    for path in (5, 0, 6):
-        for bps in (2, 3, 4, 5, 6, 8):
-            print(json.dumps({"probe": names[path], "warps_per_sm": 8 * bps, "slab_rows": rows,
-                              "gbs": round(gather_ceiling(dev, rows, path=path, blocks_per_sm=bps), 1)}), flush=True)
-    for path, name in ((7, "ldg x8, 8-byte lanes"), (8, "ldg x16, 8-byte lanes")):   # 256-byte rows
-        for bps in (4, 5, 6, 8):
-            print(json.dumps({"probe": name, "warps_per_sm": 8 * bps, "slab_rows": rows,
-                              "gbs": round(gather_ceiling(dev, rows, path=path, blocks_per_sm=bps), 1)}), flush=True)
-    for slab in (32768, 83344, 124000, 166688, 250000):     # the step kernel's point: 40 warps, 4 loads in flight
-        print(json.dumps({"probe": names[5], "warps_per_sm": 40, "slab_rows": slab, "slab_mb": round(slab * 512 / 1e6, 1),
-                          "gbs": round(gather_ceiling(dev, slab, path=5, blocks_per_sm=5), 1)}), flush=True)
+    for bps in (2, 3, 4, 5, 6, 8):
+        print(json.dumps({"probe": "ldg 16 B per lane, 8 rows in flight", "warps_per_sm": 8 * bps, "slab_rows": rows,
+                          "gbs": round(gather_ceiling(dev, rows, blocks_per_sm=bps), 1)}), flush=True)
 
 
 def inmap_arm(args):
@@ -333,22 +324,20 @@ def inmap_arm(args):
 
 
 def train_batch(inst, batch, seed):
-    """Configuration 5's synthetic batch: boards, policy targets softmax(N(0, 1)) over ~30 random legal moves,
-    WDL one-hots drawn 0.45 / 0.10 / 0.45, q uniform in [-1, 1]; as device tensors (x, pi, legal, wdl, q)."""
+    """Configuration 5's synthetic batch: boards, policy targets softmax(N(0, 1)) over 30 random legal moves of
+    the 4,168, WDL one-hots drawn 0.45 / 0.10 / 0.45, q uniform in [-1, 1]; as pinned host tensors in the
+    order of ``alphafly_b200.train.Batch`` (x, moves, probs, valid, wdl, q)."""
     from alphafly_b200 import synth
     from alphafly_b200.encoding import N_MOVES
     rng = np.random.default_rng(seed)
     x = synth.boards(batch, seed)
-    legal = np.zeros((batch, N_MOVES), bool)
-    pi = np.zeros((batch, N_MOVES), np.float32)
-    for b in range(batch):
-        idx = rng.choice(N_MOVES, size=30, replace=False)
-        z = np.exp(rng.standard_normal(30))
-        legal[b, idx] = True
-        pi[b, idx] = z / z.sum()
+    moves = np.stack([rng.choice(N_MOVES, size=30, replace=False) for _ in range(batch)]).astype(np.int64)
+    z = np.exp(rng.standard_normal((batch, 30)))
+    probs = (z / z.sum(1, keepdims=True)).astype(np.float32)
+    valid = np.ones((batch, 30), bool)
     wdl = rng.choice(3, size=batch, p=[0.45, 0.10, 0.45])
     q = rng.uniform(-1, 1, batch).astype(np.float32)
-    return tuple(torch.from_numpy(a).pin_memory() for a in (x, pi, legal, wdl, q))
+    return tuple(torch.from_numpy(a).pin_memory() for a in (x, moves, probs, valid, wdl, q))
 
 
 def train_arm(args, rank, world, local):
@@ -356,7 +345,7 @@ def train_arm(args, rank, world, local):
     AdamW; with N GPUs the gradients are averaged over NCCL) per step on B positions per GPU."""
     from alphafly_b200 import synth
     from alphafly_b200.model import FlyChessNet, ModelConfig
-    from alphafly_b200.train import TrainConfig, attach_data_parallel, make_optimizer, train_step
+    from alphafly_b200.train import Batch, TrainConfig, attach_data_parallel, make_optimizer, train_step
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     inst = workload()
@@ -376,7 +365,7 @@ def train_arm(args, rank, world, local):
     stream = torch.cuda.current_stream(dev)
 
     def step():
-        batch = tuple(t.to(dev, non_blocking=True) for t in host)    # the batch arrives from pinned host memory
+        batch = Batch(*(t.to(dev, non_blocking=True) for t in host))    # the batch arrives from pinned host memory
         return train_step(net, opt, batch, dev, q_ratio=0.5, data_parallel=world > 1)
 
     def barrier():
@@ -564,10 +553,8 @@ def main():
     rnn = rnn.to(dev)
     in_idx, out_idx = inst.in_idx.to(dev), inst.out_idx.to(dev)
     B = args.batch
-    # this rank's shard of positions: its own seed
-    u_host = torch.from_numpy(synth.drive(inst, min(B, 2048), seed=1000 + rank)).half()
-    reps = (B + u_host.shape[1] - 1) // u_host.shape[1]
-    u_host = u_host.repeat(1, reps)[:, :B].contiguous()
+    # this rank's shard of positions: its own seed (2,048 distinct positions repeated to B columns)
+    u_host = torch.from_numpy(synth.config3_drive(inst, B, rank))
     u = u_host.to(dev)
     cone = rnn.light_cone(in_idx, out_idx, STEPS_T)
     stream = torch.cuda.current_stream(dev)

@@ -130,11 +130,13 @@ AFB_API int afb_cone_forward_timed(const afb_cone *cone, int mode, const void *u
  * or their serving loop cannot take cudaMalloc's implicit synchronisation).  No counterpart in the
  * reference, which always allocates through torch.  The state lives in a fixed 32 MiB device array
  * built into the library (held on every GPU that loads it until the process exits); a cone and batch
- * whose afb_cone_forward_workspace() exceeds 32 MiB are rejected with AFB_EINVAL.  The first call on a
- * device resolves that array's device address (cudaGetSymbolAddress) and should come before any stream
- * capture on that device.  The array needs no clearing (every step overwrites what the next reads).
- * All calls on a device share it: calls whose work overlaps on the GPU (other streams, other cones)
- * race and corrupt each other's results; order them. */
+ * whose afb_cone_forward_workspace() exceeds 32 MiB are rejected with AFB_EINVAL.  The current device
+ * and `stream`'s device must be the device the cone was created on (AFB_EINVAL otherwise).  The first call
+ * on a device resolves that array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture on that device; the address is cached for the life of the process, so the call must not
+ * be used across a cudaDeviceReset of that device.  The array needs no clearing (every step overwrites
+ * what the next reads).  All calls on a device share it: calls whose work overlaps on the GPU (other
+ * streams, other cones) race and corrupt each other's results; order them. */
 AFB_API int afb_cone_forward_noalloc(const afb_cone *cone, int mode, const void *u_in, int64_t ld_u, int64_t batch,
                                      float *out, int64_t ld_out, void *stream);
 

@@ -1,5 +1,6 @@
-"""The C ABI: every entry point declared in include/*.h is exported by libafb.so and bound by the
-Python host, and argument errors come back as AfbError without touching a GPU."""
+"""The C ABI: every entry point declared in include/afb.h is exported by libafb.so and bound by the
+Python host, bench.py's probe lives in its own library (include/afb_probe.h), and argument errors come
+back as AfbError without touching a GPU."""
 
 import ctypes
 import os
@@ -28,6 +29,20 @@ def test_library_exports_every_declared_symbol():
         assert hasattr(lib, name), name
         assert name in _lib.SIGNATURES, f"{name} has no Python binding"
     assert lib.afb_compiled_arch() == 100 and lib.afb_version() >= 1
+
+
+def test_probe_is_a_separate_library():
+    from alphafly_b200 import _lib
+    lib = _lib.load()
+    assert not hasattr(lib, "afb_probe_gather")
+    probe = _lib.load_probe()
+    text = open(os.path.join(ROOT, "include", "afb_probe.h")).read()
+    names = sorted(set(re.findall(r"AFB_PROBE_API\s+[\w\s\*]*?\b(afb_\w+)\s*\(", text)))
+    assert names == sorted(_lib.PROBE_SIGNATURES)
+    for name in names:
+        assert hasattr(probe, name), name
+    # argument checks come before any device call
+    assert probe.afb_probe_gather(9, None, 1, None, 1, None, 0, None) == -1
 
 
 def test_argument_errors_are_reported_without_a_gpu():

@@ -71,20 +71,24 @@ def _bucketed(rank, world, port, out):
     torch.manual_seed(0)                                  # the same model on both ranks
     net = torch.nn.Sequential(torch.nn.Linear(6, 40), torch.nn.Tanh(), torch.nn.Linear(40, 30), torch.nn.Tanh(),
                               torch.nn.Linear(30, 2))
-    unused = torch.nn.Parameter(torch.zeros(4))           # takes no gradient
-    params = [p for m in reversed(net) for p in reversed(list(m.parameters()))] + [unused]
+    unused = torch.nn.Parameter(torch.zeros(4))           # takes no gradient on any rank
+    sometimes = torch.nn.Parameter(torch.ones(3))         # takes a gradient on rank 0 only
+    params = [p for m in reversed(net) for p in reversed(list(m.parameters()))] + [sometimes, unused]
     x = torch.randn(8, 6, generator=torch.Generator().manual_seed(20 + rank))
     net(x).square().sum().backward()
-    local = [p.grad.clone() for p in params[:-1]]
-    for p in params[:-1]:
+    local = [p.grad.clone() for p in params[:-2]]
+    for p in params[:-2]:
         p.grad = None
     red = BucketedAllReduce(params, bucket_mb=0.003)        # ~3 KB: several buckets
     red.arm()
-    net(x).square().sum().backward()
+    loss = net(x).square().sum()
+    if rank == 0:
+        loss = loss + (sometimes * torch.arange(3.0)).sum()
+    loss.backward()
     in_backward = red.launched_in_backward
     red.finish()
-    out[rank] = {"local": local, "avg": [p.grad.clone() for p in params[:-1]], "unused": unused.grad,
-                 "buckets": len(red.buckets), "in_backward": in_backward}
+    out[rank] = {"local": local, "avg": [p.grad.clone() for p in params[:-2]], "unused": unused.grad,
+                 "sometimes": sometimes.grad, "buckets": len(red.buckets), "in_backward": in_backward}
     dist.destroy_process_group()
 
 
@@ -98,6 +102,8 @@ def test_bucketed_all_reduce_overlaps_the_backward_and_averages():
         r = res[rank]
         assert r["buckets"] >= 3 and r["in_backward"] >= r["buckets"] - 1, r   # all but the unused one
         assert r["unused"] is None
+        # a gradient present on one rank only: both ranks step it with the mean (zeros for the other rank)
+        torch.testing.assert_close(r["sometimes"], torch.arange(3.0) / 2)
         for k, g in enumerate(r["avg"]):
             torch.testing.assert_close(g, (res[0]["local"][k] + res[1]["local"][k]) / 2)
 

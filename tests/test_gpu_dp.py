@@ -26,7 +26,7 @@ def _dp_rank(rank, world, port, out, bucketed):
     from conftest import golden
     from alphafly_b200 import synth
     from alphafly_b200.model import FlyChessNet, ModelConfig
-    from alphafly_b200.train import Sample, TrainConfig, attach_data_parallel, losses, average_gradients, collate
+    from alphafly_b200.train import Sample, attach_data_parallel, average_gradients, loss_terms, make_batch
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
@@ -40,8 +40,7 @@ def _dp_rank(rank, world, port, out, bucketed):
     share = range(rank * n // world, (rank + 1) * n // world)
     batch = [Sample(g["batch_x"][i], g["batch_idx"][i].astype(np.int64), g["batch_pi"][i], float(g["batch_q"][i]),
                     int(g["batch_wdl"][i])) for i in share]
-    x, pi, legal, wdl, q = collate(batch, "cuda")
-    pl, vl, _ = losses(net, x, pi, legal, wdl, q, 0.5)
+    pl, vl, _ = loss_terms(net, make_batch(batch, "cuda"), 0.5)
     if bucketed:                                  # train_step's path: buckets all-reduced during the backward
         red = net.grad_reducer
         red.arm()

@@ -72,3 +72,58 @@ def test_noalloc_forward_refuses_a_batch_beyond_its_scratch(cone_and_inputs):
     rc = lib.afb_cone_forward_noalloc(cone._h, _lib.MODE_F32, _ptr(u), big, big, _ptr(u), big, stream)
     assert rc == _lib.EINVAL
     assert b"built-in scratch" in lib.afb_last_error()
+
+
+def test_noalloc_forward_allocates_nothing(cone_and_inputs):
+    """Warm calls change neither the device's free memory (no cudaMalloc behind the caller's back) nor
+    torch's allocator statistics."""
+    cone, u, _ = cone_and_inputs
+    x = u.half()
+    out = torch.empty(cone.n_out, x.shape[1], device=DEV)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    lib = _lib.load()
+    _lib.check(lib.afb_cone_forward_noalloc(cone._h, _lib.MODE_DEV16, _ptr(x), x.stride(0), x.shape[1], _ptr(out),
+                                            out.stride(0), stream))
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    stats_before = torch.cuda.memory_stats()
+    for _ in range(5):
+        _lib.check(lib.afb_cone_forward_noalloc(cone._h, _lib.MODE_DEV16, _ptr(x), x.stride(0), x.shape[1], _ptr(out),
+                                                out.stride(0), stream))
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    stats_after = torch.cuda.memory_stats()
+    assert free_after == free_before
+    for key in ("allocation.all.allocated", "segment.all.allocated", "allocated_bytes.all.current"):
+        assert stats_after.get(key) == stats_before.get(key), key
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_noalloc_forward_on_a_second_device_and_device_checks():
+    """A cone on cuda:1 runs against cuda:1's copy of the scratch; called with another device current, or
+    with another device's stream, it is refused before any launch."""
+    inst = synth.small()
+    rnn = ConnectomeRNN(inst.conn)
+    synth.apply(rnn, inst)
+    dev1 = torch.device("cuda", 1)
+    rnn = rnn.to(dev1)
+    in_idx, out_idx = inst.in_idx.to(dev1), inst.out_idx.to(dev1)
+    u = torch.from_numpy(synth.drive(inst, 200, seed=5)).to(dev1).half()
+    lib = _lib.load()
+    with torch.no_grad(), torch.cuda.device(dev1):
+        ref = rnn.forward_io(u, in_idx, out_idx, 6)
+        cone = rnn.light_cone(in_idx, out_idx, 6)
+        out = torch.full((cone.n_out, u.shape[1]), float("nan"), device=dev1)
+        s1 = ctypes.c_void_p(torch.cuda.current_stream(dev1).cuda_stream)
+        _lib.check(lib.afb_cone_forward_noalloc(cone._h, _lib.MODE_DEV16, _ptr(u), u.stride(0), u.shape[1], _ptr(out),
+                                                out.stride(0), s1))
+        torch.cuda.synchronize(dev1)
+        assert orc.rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
+        s0 = ctypes.c_void_p(torch.cuda.current_stream(torch.device("cuda", 0)).cuda_stream)
+        rc = lib.afb_cone_forward_noalloc(cone._h, _lib.MODE_DEV16, _ptr(u), u.stride(0), u.shape[1], _ptr(out),
+                                          out.stride(0), s0)
+        assert rc == _lib.EINVAL and b"stream belongs to device 0" in lib.afb_last_error()
+    with torch.cuda.device(0):
+        rc = lib.afb_cone_forward_noalloc(cone._h, _lib.MODE_DEV16, _ptr(u), u.stride(0), u.shape[1], _ptr(out),
+                                          out.stride(0), s1)
+        assert rc == _lib.EINVAL and b"is not the cone's device" in lib.afb_last_error()
