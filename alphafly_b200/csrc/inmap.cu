@@ -23,14 +23,20 @@
 //     stores.
 // Every mbarrier wait is bounded: a wait that gives up sets *status (the host reads it) and the CTA
 // skips ahead instead of hanging; TMEM is always released.  No cluster, no multicast.
-#include <cudaTypedefs.h>
-
 #include <cstring>
 
-#include "common.cuh"
+#include "tc.cuh"
 
 namespace afb {
 namespace {
+
+using tc::bar_init;
+using tc::bar_wait;
+using tc::fail;
+using tc::kBK;
+using tc::kMmaK;
+using tc::smem_desc;
+using tc::tma_load;
 
 #ifndef AFB_INMAP_SUB
 #define AFB_INMAP_SUB 2
@@ -39,8 +45,6 @@ constexpr int kBM = 128;                        // neurons per MMA (TMEM lanes)
 constexpr int kSub = AFB_INMAP_SUB;             // MMA tiles per CTA along the neurons
 constexpr int kRows = kSub * kBM;               // neurons per CTA
 constexpr int kBN = 256;                        // positions per CTA (TMEM columns per sub-tile)
-constexpr int kBK = 64;                         // 64 float16 = one 128-byte swizzle row
-constexpr int kMmaK = 16;                       // K of one tcgen05.mma kind::f16
 // one CTA per SM with two sub-tiles (3 stages of 64 KB); with one, two CTAs per SM of 2 stages of 48 KB
 constexpr int kStages = kSub == 2 ? 3 : 2;
 constexpr int kThreads = 128 * kSub;            // one epilogue warp per (TMEM lane quarter, sub-tile)
@@ -50,41 +54,7 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kSmemBytes = kStages * kStageBytes + 1024 /* barriers */ + 1024 /* alignment slack */;
 constexpr uint32_t kTmemCols = kSub * kBN;      // float32 accumulators: one column per position and sub-tile
 static_assert(kSub == 1 || kSub == 2, "one or two MMA tiles per CTA");
-constexpr uint32_t kWaitLimit = 1u << 22;
-
-// Instruction descriptor of tcgen05.mma kind::f16: D float32 (bits 4-5 = 1), A and B float16 (bits 7-9,
-// 10-12 = 0), both K-major (bits 15, 16 = 0), N >> 3 in bits 17-22, M >> 4 in bits 24-28.
-constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kBN >> 3) << 17) | ((uint32_t)(kBM >> 4) << 24);
-
-// Shared-memory descriptor of a K-major SWIZZLE_128B operand tile whose rows are 128 bytes and whose
-// 8-row groups are 1024 bytes apart: start address >> 4 (bits 0-13), leading byte offset 16 B >> 4
-// (bits 16-29, unused by this layout), stride byte offset 1024 B >> 4 (bits 32-45), descriptor version 1
-// (bits 46-47), swizzle mode 2 = 128 B (bits 61-63).  The tile base is 1024-byte aligned.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr) {
-    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) |
-           ((uint64_t)2 << 61);
-}
-
-__device__ __forceinline__ void bar_init(uint32_t bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ bool bar_wait(uint32_t bar, uint32_t parity) {
-    for (uint32_t it = 0; it < kWaitLimit; ++it) {
-        uint32_t ok;
-        asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-                     : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-        if (ok) return true;
-    }
-    return false;
-}
-__device__ __forceinline__ void fail(int *status, int code) {
-    if (status) atomicOr(status, code);
-}
-
-__device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap *map, int x, int y, uint32_t bar) {
-    asm volatile("cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"
-                 ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar) : "memory");
-}
+constexpr uint32_t kIdesc = tc::idesc_f16(kBM, kBN);
 
 __device__ __forceinline__ void tma_store(const CUtensorMap *map, int x, int y, uint32_t src) {
     asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];\n"
@@ -241,6 +211,23 @@ __global__ void __launch_bounds__(kThreads, 1) input_map_kernel(const __grid_con
     }
 }
 
+// The output u: n_in rows x batch float16 columns, row stride ldu elements, boxes of 128 rows x 32 columns
+// staged SWIZZLE_64B.
+void encode_output(CUtensorMap *map, void *base, int64_t n_in, int64_t batch, int64_t ldu) {
+    const cuuint64_t dim[2] = {(cuuint64_t)batch, (cuuint64_t)n_in};
+    const cuuint64_t stride[1] = {(cuuint64_t)ldu * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kChunkCols, (cuuint32_t)kBM};
+    const cuuint32_t estride[2] = {1, 1};
+    const CUresult r = tc::tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dim, stride, box, estride,
+                                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
+                                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AFB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output) failed with code " + std::to_string((int)r));
+}
+
+}  // namespace
+
+namespace tc {
+
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
     if (!encode) {
@@ -253,7 +240,6 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     return encode;
 }
 
-// A K-major float16 operand: rows x k_dim elements, row stride ld elements, boxes of box_rows x 64.
 void encode_operand(CUtensorMap *map, const void *base, int64_t rows, int64_t k_dim, int64_t ld, uint32_t box_rows) {
     const cuuint64_t dim[2] = {(cuuint64_t)k_dim, (cuuint64_t)rows};
     const cuuint64_t stride[1] = {(cuuint64_t)ld * 2};
@@ -265,20 +251,7 @@ void encode_operand(CUtensorMap *map, const void *base, int64_t rows, int64_t k_
     AFB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed with code " + std::to_string((int)r));
 }
 
-// The output u: n_in rows x batch float16 columns, row stride ldu elements, boxes of 128 rows x 32 columns
-// staged SWIZZLE_64B.
-void encode_output(CUtensorMap *map, void *base, int64_t n_in, int64_t batch, int64_t ldu) {
-    const cuuint64_t dim[2] = {(cuuint64_t)batch, (cuuint64_t)n_in};
-    const cuuint64_t stride[1] = {(cuuint64_t)ldu * 2};
-    const cuuint32_t box[2] = {(cuuint32_t)kChunkCols, (cuuint32_t)kBM};
-    const cuuint32_t estride[2] = {1, 1};
-    const CUresult r = tensor_map_encoder()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dim, stride, box, estride,
-                                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B,
-                                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    AFB_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (output) failed with code " + std::to_string((int)r));
-}
-
-}  // namespace
+}  // namespace tc
 }  // namespace afb
 
 using namespace afb;
@@ -296,8 +269,8 @@ extern "C" int afb_input_map_f16(int64_t n_in, int64_t batch, int64_t k_dim, con
         AFB_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
                   "W and x must be 16-byte aligned");
         CUtensorMap map_w, map_x, map_u;
-        encode_operand(&map_w, w, n_in, k_dim, ldw, kRows);
-        encode_operand(&map_x, x, batch, k_dim, ldx, kBN);
+        tc::encode_operand(&map_w, w, n_in, k_dim, ldw, kRows);
+        tc::encode_operand(&map_x, x, batch, k_dim, ldx, kBN);
         const int tma_out = (ldu % 8 == 0 && (reinterpret_cast<uintptr_t>(u) & 15) == 0) ? 1 : 0;
         if (tma_out) encode_output(&map_u, u, n_in, batch, ldu);
         else std::memset(&map_u, 0, sizeof(map_u));

@@ -11,8 +11,9 @@ the data path, weak scaling.  ``value`` = positions evaluated by all ranks / max
 time of the K timed steps (inputs resident in HBM); ``e2e`` = the same through the public call with
 the drive in pinned host memory and the output copied back inside the timed region.
 
-``--impl reference`` times the reference algorithm's CPU implementation (the float32 port in
-oracle/, all host threads) on a bounded sample of the same workload and prints the same line.
+``--impl reference`` times the reference's CPU implementation of the path (its torch CPU sparse forward_io,
+restated with the same calls in oracle/torch_port.py, all host threads) on 256-position samples of the
+same workload and prints the same line.
 ``--train`` times configuration 5 instead (FlyChessNet train_step, B = 2,048 per GPU, data parallel over
 NCCL under torchrun); ``--probe`` prints the device's gather ceiling against warps per SM; ``--evaluator``
 times self-play evaluation rounds (B = 1,120 positions) through three implementations of the Evaluator.
@@ -205,57 +206,84 @@ def init_dist(args):
     return rank, world, local
 
 
-def cpu_sample(inst, seconds, batch=16):
-    """The oracle's float32 forward (OpenMP, all host threads) on ``batch`` positions, repeated for about
-    ``seconds``; returns (positions/s, threads, description)."""
+CPU_BATCH = 256
+
+
+def host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def torch_cpu_forward(inst):
+    """The reference's CPU path for configuration 3's graph: its torch CPU sparse forward_io, restated with the
+    same torch calls in oracle/torch_port.py (the reference's own source does not travel to the GPU box), on
+    every host thread."""
+    from oracle.torch_port import TorchCpuForward
+    torch.set_num_threads(host_threads())
+    return TorchCpuForward(inst.n, inst.conn.pre.numpy(), inst.conn.post.numpy(), inst.conn.sign.numpy(),
+                           inst.w0.numpy(), inst.log_gain.numpy(), inst.bias.numpy(), inst.alpha_logit.numpy(),
+                           inst.in_idx.numpy(), inst.out_idx.numpy(), STEPS_T)
+
+
+def cpu_sample(inst, seconds, batch=CPU_BATCH):
+    """The reference's CPU forward (torch CPU sparse, all host threads) on ``batch`` positions of the bench's
+    drive, repeated for about ``seconds``; and, beside it, the oracle's C/OpenMP float32 port on the same
+    positions for a third of the time.  Returns the cpu_baseline object."""
     from alphafly_b200 import synth
     from oracle import oracle as orc
-    fwd = orc.CpuForward(inst.n, inst.conn.pre.numpy(), inst.conn.post.numpy(), inst.conn.sign.numpy(), inst.w0.numpy(),
-                         inst.log_gain.numpy(), inst.bias.numpy(), inst.alpha_logit.numpy(), inst.in_idx.numpy(),
-                         inst.out_idx.numpy(), STEPS_T)
-    u = synth.drive(inst, batch, seed=123)
-    fwd(u)                                                   # warm-up
-    reps, t0 = 0, time.perf_counter()
-    while True:
-        fwd(u)
-        reps += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    threads = orc.lib().ref_num_threads()
-    return reps * batch / el, threads, (f"{reps} x {batch} positions of configuration 3's graph, float32 light-cone "
-                                        f"forward (oracle port of the reference), {el:.1f} s")
+    u = synth.config3_drive(inst, batch).astype(np.float32)
+
+    def rate(fn, budget):
+        fn(u)                                                 # warm-up
+        reps, t0 = 0, time.perf_counter()
+        while True:
+            fn(u)
+            reps += 1
+            el = time.perf_counter() - t0
+            if el >= budget:
+                return reps * batch / el, reps, el
+
+    ref = torch_cpu_forward(inst)
+    v, reps, el = rate(ref, seconds)
+    port = orc.CpuForward(inst.n, inst.conn.pre.numpy(), inst.conn.post.numpy(), inst.conn.sign.numpy(), inst.w0.numpy(),
+                          inst.log_gain.numpy(), inst.bias.numpy(), inst.alpha_logit.numpy(), inst.in_idx.numpy(),
+                          inst.out_idx.numpy(), STEPS_T, cone=ref.cone)
+    v_port, _, _ = rate(port, seconds / 3)
+    return {"value": v, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{reps} x {batch} positions of the bench drive of configuration 3, float32 light-cone forward_io "
+                      f"through torch CPU sparse CSR (the reference's CPU path, restated in oracle/torch_port.py), {el:.1f} s",
+            "c_openmp_port": {"value": v_port, "unit": UNIT, "threads": orc.lib().ref_num_threads(),
+                              "what": "oracle/csr_ref.c fused float32 step (OpenMP), same positions"}}
 
 
 def reference_arm(args, rank, world):
+    """The reference's CPU implementation of the path (torch CPU sparse forward_io, oracle/torch_port.py) on
+    the host cores: one step = one forward of CPU_BATCH positions of the bench drive.  Rank 0 only."""
     if rank != 0:
         return
-    inst = workload()
-    per_step = []
-    from oracle import oracle as orc
     from alphafly_b200 import synth
-    batch = 16
-    fwd = orc.CpuForward(inst.n, inst.conn.pre.numpy(), inst.conn.post.numpy(), inst.conn.sign.numpy(), inst.w0.numpy(),
-                         inst.log_gain.numpy(), inst.bias.numpy(), inst.alpha_logit.numpy(), inst.in_idx.numpy(),
-                         inst.out_idx.numpy(), STEPS_T)
-    u = synth.drive(inst, batch, seed=123)
+    inst = workload()
+    fwd = torch_cpu_forward(inst)
+    u = synth.config3_drive(inst, CPU_BATCH).astype(np.float32)
     for _ in range(args.warmup):
         fwd(u)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        t = time.perf_counter()
         fwd(u)
-        per_step.append(time.perf_counter() - t)
     el = time.perf_counter() - t0
-    value = args.steps * batch / el
-    threads = orc.lib().ref_num_threads()
+    value = args.steps * CPU_BATCH / el
+    threads = torch.get_num_threads()
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1000 * el / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config3: full-scale synthetic connectome, 6-step light-cone forward",
-                       "batch_per_step": batch, "note": "each step is a bounded sample of the GPU arm's 35,840-position batch"},
+                       "batch_per_step": CPU_BATCH,
+                       "note": "each step is a bounded sample of the GPU arm's 35,840-position batch"},
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"{batch} positions per step, float32, oracle port of chessfly/brain.py forward_io"},
+                             "sample": f"{CPU_BATCH} positions per step, float32, the reference's torch CPU sparse "
+                                       "forward_io restated with the same torch calls (oracle/torch_port.py)"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -681,8 +709,7 @@ def main():
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        v, threads, desc = cpu_sample(inst, args.cpu_seconds)
-        cpu = {"value": v, "unit": UNIT, "cores": threads, "kind": "port", "sample": desc}
+        cpu = cpu_sample(inst, args.cpu_seconds)
 
     if world > 1:
         torch.distributed.barrier()

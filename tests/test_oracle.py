@@ -207,3 +207,19 @@ def test_planted_mistake_in_the_oracle_is_caught():
     cone.ops[3].edges = cone.ops[3].edges[1:]
     with pytest.raises(AssertionError):
         check_cone_arrays(cone, g, "cone4")
+
+
+@pytest.mark.parametrize("config", ["small", "shuffled"])
+def test_torch_cpu_restatement_matches_reference(config):
+    """oracle/torch_port.py (the reference's torch CPU sparse forward_io, timed as the CPU baseline) against
+    the reference's own float32 outputs."""
+    from oracle.torch_port import TorchCpuForward
+    g = golden(config)
+    inst = synth.small() if config == "small" else synth.shuffled()
+    fwd = TorchCpuForward(inst.n, inst.conn.pre.numpy(), inst.conn.post.numpy(), inst.conn.sign.numpy(), inst.w0.numpy(),
+                          inst.log_gain.numpy(), inst.bias.numpy(), inst.alpha_logit.numpy(), inst.in_idx.numpy(),
+                          inst.out_idx.numpy(), 6)
+    batch, seed = (64, 0) if config == "small" else (16, 3)
+    out = fwd(synth.drive(inst, batch, seed=seed)).numpy()
+    assert out.dtype == np.float32 and out.shape == (len(inst.out_idx), batch)
+    assert orc.rel_l2(out, g["fwd_io_f32"]) < 1e-5
