@@ -53,8 +53,11 @@ SIGNATURES = {
     "afb_graph_destroy": (None, [_p]),
     "afb_graph_forward_workspace": (_sz, [_p, _i64]),
     "afb_graph_forward": (_int, [_p, _p, _p, _p, _f, _p, _i64, _i64, _int, _p, _i64, _p, _sz, _p]),
-    "afb_legal_logits": (_int, [_i64, _p, _p, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _p, _p, _p, _p, _p]),
     "afb_input_map_f16": (_int, [_i64, _i64, _i64, _p, _i64, _p, _i64, _p, _f, _p, _i64, _p, _p]),
+    "afb_heads_split": (_int, [_i64, _i64, _p, _i64, _p, _p, _i64, _p]),
+    "afb_readout_workspace": (_sz, [_i64, _i64]),
+    "afb_readout_heads": (_int, [_i64, _i64, _p, _i64, _p, _p, _f, _f, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _int, _p,
+                                 _i64, _p, _sz, _p, _p]),
 }
 
 # the entry points of include/afb_probe.h (libafb_probe.so)

@@ -8,8 +8,10 @@ reference's names, parameters, buffers and state_dict keys (chessfly/model.py:26
 load unchanged.  The recurrence runs in ``alphafly_b200.brain`` (libafb).  The input map writes the
 (sensory neurons, batch) layout the recurrence reads in one GEMM (W x^T scaled by the input gain),
 instead of x W^T followed by a transpose copy: for float16 inference in libafb's tensor-core kernel
-(``input_map_f16``), in float32 (training, the float32 path) through cuBLAS.  The heads are cuBLAS GEMMs,
-and the Evaluator's legal-move logits a libafb kernel.
+(``input_map_f16``), in float32 (training, the float32 path) through cuBLAS.  In inference the normaliser
+and the heads are one tensor-core readout in libafb (``FlyChessNet.heads``: the factorised from/to terms
+folded into the policy rows, float32 accuracy from split float16 operands); training keeps the float32
+layers, whose gradients autograd takes.
 """
 
 from __future__ import annotations
@@ -133,18 +135,85 @@ class FlyChessNet(nn.Module):
             st = self._status = torch.zeros(1, dtype=torch.int32, device=device)
         return st
 
+    def brain_output(self, x: torch.Tensor) -> torch.Tensor:
+        """x: (B, N_FEATURES) -> the output neurons after the recurrence, (len(out_idx), B) float32
+        (chessfly/model.py:97-103 up to the normaliser)."""
+        dtype = self.infer_dtype if x.is_cuda and not torch.is_grad_enabled() else torch.float32
+        u_in = self.drive(x, dtype)
+        return self.brain.forward_io(u_in, self.in_idx, self.out_idx, self.cfg.steps)
+
     def readout(self, x: torch.Tensor) -> torch.Tensor:
         """x: (B, N_FEATURES) -> the normalised output-neuron state r (B, len(out_idx)) the heads read
         (chessfly/model.py:97-103)."""
-        dtype = self.infer_dtype if x.is_cuda and not torch.is_grad_enabled() else torch.float32
-        u_in = self.drive(x, dtype)
-        return self.norm(self.brain.forward_io(u_in, self.in_idx, self.out_idx, self.cfg.steps).T.float())
+        return self.norm(self.brain_output(x).T.float())
 
     def forward(self, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """x: (B, N_FEATURES) -> policy logits (B, N_MOVES), WDL logits (B, 3)."""
-        r = self.readout(x)
+        """x: (B, N_FEATURES) -> policy logits (B, N_MOVES), WDL logits (B, 3).  Inference on a GPU with the
+        normaliser in eval mode runs the normaliser and the heads as one tensor-core readout (``heads``);
+        training (and a normaliser still collecting statistics) keeps the float32 layers."""
+        if x.is_cuda and not torch.is_grad_enabled() and not self.norm.training:
+            return self.heads(self.brain_output(x))
+        return self.dense_heads(self.readout(x))
+
+    def dense_heads(self, r: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """The heads as the reference's float32 layers on the normalised state r (B, len(out_idx))
+        (chessfly/model.py:104-105); the training path, through which autograd runs."""
         logits = self.policy(r) + self.policy_from(r)[:, self.move_from] + self.policy_to(r)[:, self.move_to]
         return logits, self.value(r)
+
+    @torch.no_grad()
+    def folded_heads(self) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        """(W_hi, W_lo, bias) of the tensor-core readout: the policy rows with the factorised from/to terms
+        folded in (W[m] = Wp[m] + Wf[move_from[m]] + Wt[move_to[m]], exact by linearity), then the value
+        rows, as float16 hi / scaled lo parts (``afb_heads_split``) with 16-byte rows, and the float32 bias.
+        Rewritten in place when a head parameter changed, so a captured CUDA graph reading them stays valid."""
+        layers = (self.policy, self.policy_from, self.policy_to, self.value)
+        params = [t for layer in layers for t in (layer.weight, layer.bias)]
+        key = tuple(t._version for t in params)
+        where = tuple(t.data_ptr() for t in params)
+        c = getattr(self, "_heads16", None)
+        if c is not None and c[0] == key and c[1] == where:
+            return c[2], c[3], c[4]
+        w = torch.cat([self.policy.weight + self.policy_from.weight[self.move_from] + self.policy_to.weight[self.move_to],
+                       self.value.weight]).float().contiguous()
+        b = torch.cat([self.policy.bias + self.policy_from.bias[self.move_from] + self.policy_to.bias[self.move_to],
+                       self.value.bias]).float().contiguous()
+        rows, n_out = w.shape
+        ldw = -(-n_out // 8) * 8
+        if c is None or c[1] != where or c[2].shape != (rows, ldw):
+            hi = torch.empty(rows, ldw, dtype=torch.float16, device=w.device)
+            lo = torch.empty_like(hi)
+            bias = torch.empty(rows, dtype=torch.float32, device=w.device)
+        else:
+            hi, lo, bias = c[2], c[3], c[4]
+        bias.copy_(b)
+        with torch.cuda.device(w.device):
+            _lib.call("afb_heads_split", rows, n_out, w.data_ptr(), n_out, hi.data_ptr(), lo.data_ptr(), ldw,
+                      torch.cuda.current_stream(w.device).cuda_stream)
+        self._heads16 = (key, where, hi, lo, bias)
+        return hi, lo, bias
+
+    @torch.no_grad()
+    def heads(self, out: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """The readout on the tensor cores: out (len(out_idx), B) float32, the recurrence's output, ->
+        policy logits (B, N_MOVES) and WDL logits (B, 3), float32 (``afb_readout_heads``: RunningNorm with
+        the running statistics, then the folded heads at float32 accuracy)."""
+        hi, lo, bias = self.folded_heads()
+        n_out, batch = out.shape
+        out = out if out.dtype == torch.float32 and out.stride(1) == 1 else out.float().contiguous()
+        dev = out.device
+        logits = torch.empty(batch, N_MOVES, dtype=torch.float32, device=dev)
+        wdl = torch.empty(batch, 3, dtype=torch.float32, device=dev)
+        lib = _lib.load()
+        ws = torch.empty(lib.afb_readout_workspace(batch, n_out), dtype=torch.uint8, device=dev)
+        norm = self.norm
+        with torch.cuda.device(dev):
+            _lib.check(lib.afb_readout_heads(n_out, batch, out.data_ptr(), out.stride(0), norm.mean.data_ptr(),
+                                             norm.var.data_ptr(), float(norm.eps), float(norm.clip), hi.shape[0], N_MOVES,
+                                             hi.data_ptr(), lo.data_ptr(), hi.shape[1], bias.data_ptr(), logits.data_ptr(),
+                                             N_MOVES, 0, wdl.data_ptr(), 3, ws.data_ptr(), ws.numel(),
+                                             self._map_status(dev).data_ptr(), torch.cuda.current_stream(dev).cuda_stream))
+        return logits, wdl
 
     @staticmethod
     def expected_value(wdl_logits: torch.Tensor) -> torch.Tensor:
@@ -213,8 +282,9 @@ class Evaluator:
         captured once per batch bucket (multiples of 256 positions, the step kernel's batch tile; at most
         ``max_graphs`` kept); the weight-dependent constants are refreshed before a replay when a
         parameter changed, so training between rounds is seen;
-      - legal-move logits come from ``afb_legal_logits``: only the requested dot products, instead of the
-        dense (B, 4168) product and a gather.
+      - the readout is libafb's tensor-core kernel (``FlyChessNet.heads``, part of the graph): the dense
+        (B, 4168) logits at float32 accuracy, from which the legal entries are gathered, or which are
+        rounded to float16 for the lazy search.
     """
 
     BUCKET = 256
@@ -247,15 +317,18 @@ class Evaluator:
 
     # -- the network -------------------------------------------------------------------------------------
     def _trunk(self, x: torch.Tensor):
+        """Features -> (policy logits (B, N_MOVES) float32, values (B,)): the recurrence and the tensor-core
+        readout."""
         net = self.net
-        r = net.readout(x)
-        return r, net.policy_from(r), net.policy_to(r), net.expected_value(net.value(r).float())
+        logits, wdl = net.heads(net.brain_output(x))
+        return logits, net.expected_value(wdl)
 
     def _refresh_constants(self) -> None:
         net, brain = self.net, self.net.brain
         mode = _lib.MODE_DEV16 if net.infer_dtype == torch.float16 else _lib.MODE_F32
         if mode == _lib.MODE_DEV16:
             net.half_encoder()
+        net.folded_heads()
         cone = brain.light_cone(net.in_idx, net.out_idx, net.cfg.steps)
         cone.set_weights(brain, mode, brain._weight_key(mode, cone))
 
@@ -308,29 +381,22 @@ class Evaluator:
         x_dev = self._stage(slot, "x", np.asarray(x, np.float16), torch.float16).view(b, -1)
         if self.graphs and x_dev.is_cuda and b > 0:
             self._refresh_constants()
-            g, x_static, (r, f, t, values) = self._graph((b + self.BUCKET - 1) // self.BUCKET * self.BUCKET)
+            g, x_static, (logits, values) = self._graph((b + self.BUCKET - 1) // self.BUCKET * self.BUCKET)
             x_static[:b].copy_(x_dev)
             g.replay()
-            r, f, t, values = r[:b], f[:b], t[:b], values[:b]
+            logits, values = logits[:b], values[:b]
         else:
-            r, f, t, values = self._trunk(x_dev)
+            logits, values = self._trunk(x_dev)
         if rows is None:
-            out = (net.policy(r) + f[:, net.move_from] + t[:, net.move_to]).half().reshape(-1)
+            out = logits.half().reshape(-1)
         else:
+            if len(rows) != len(cols):
+                raise ValueError("rows and cols must have the same length")
+            if len(rows) and (np.min(rows) < 0 or np.max(rows) >= b or np.min(cols) < 0 or np.max(cols) >= N_MOVES):
+                raise ValueError(f"legal-move indices out of range: rows in [0, {b}), cols in [0, {N_MOVES})")
             rows_dev = self._stage(slot, "rows", np.asarray(rows, np.int64), torch.int64)
             cols_dev = self._stage(slot, "cols", np.asarray(cols, np.int64), torch.int64)
-            out = torch.empty(len(rows_dev), dtype=torch.float32, device=self.device)
-            if out.is_cuda:
-                lib = _lib.load()
-                w, bias = net.policy.weight.detach(), net.policy.bias.detach()
-                _lib.check(lib.afb_legal_logits(len(out), rows_dev.data_ptr(), cols_dev.data_ptr(), b, r.shape[1],
-                                                r.contiguous().data_ptr(), w.shape[0], w.contiguous().data_ptr(),
-                                                bias.data_ptr(), f.shape[1], f.contiguous().data_ptr(),
-                                                t.contiguous().data_ptr(), net.move_from.data_ptr(),
-                                                net.move_to.data_ptr(), out.data_ptr(),
-                                                torch.cuda.current_stream(self.device).cuda_stream))
-            else:
-                out = (net.policy(r) + f[:, net.move_from] + t[:, net.move_to])[rows_dev, cols_dev]
+            out = logits[rows_dev, cols_dev]
         out_host = self._pinned(slot, "out_half" if rows is None else "out", out.numel(), out.dtype)
         val_host = self._pinned(slot, "values", b, torch.float32)
         out_host[:out.numel()].copy_(out, non_blocking=True)

@@ -520,7 +520,7 @@ def evaluator_arm(args):
     class Eager:                                  # chessfly/model.py:120-132, eager
         @torch.no_grad()
         def submit(self, x, rows, cols):
-            logits, wdl = net(torch.from_numpy(x).to(dev, non_blocking=True).float())
+            logits, wdl = net.dense_heads(net.readout(torch.from_numpy(x).to(dev, non_blocking=True).float()))
             legal = logits[torch.from_numpy(rows).to(dev, non_blocking=True), torch.from_numpy(cols).to(dev, non_blocking=True)]
             return legal.float(), net.expected_value(wdl.float())
 
@@ -632,11 +632,23 @@ def main():
                 "frac": round(achieved / hbm, 4), "peak_kind": peak_kind,
                 "traffic": measured_traffic() if B == 35_840 else None,
                 "traffic_source": "profiles/step_kernel_traffic_config3.txt (ncu, B = 35,840)",
-                "kernel": "step_kernel<__half,__half> (steps 2-6) and step_kernel_ring (step 1): 6 launches per forward",
+                "kernel": "step_kernel<__half,__half> (steps 3-6) and step_kernel_ring<__half,__half> (steps 1-2): "
+                          "6 launches per forward",
                 "algorithmic_bytes_per_launch": int(sum(per_step_bytes) / STEPS_T),
                 "launch_ms": [round(x, 3) for x in kernel_ms],
                 "l2_gather_bytes_per_forward": int(gathered),
                 "l2_gather_gbs": round(gathered / (kernel_total_ms / 1000.0) / 1e9, 1)}
+    # the other ceiling of the sparse path: one FMA per synapse and position (float16 weight x float16 state into
+    # a float32 sum), against the device's FP32 FMA issue rate at the SM clock sampled during the timed region
+    clk = clocks.summary()
+    sm_mhz = clk.get("sm_mhz") or clk.get("sm_max_mhz") or 1965.0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    fma_rate = sms * 128 * sm_mhz * 1e6
+    fmas = sum(cone.nnz) * B
+    roofline.update({"fma_per_forward": int(fmas), "fma_gfma_s": round(fmas / (kernel_total_ms / 1000.0) / 1e9, 1),
+                     "fma_pipe_frac": round(fmas / (kernel_total_ms / 1000.0) / fma_rate, 4),
+                     "fma_rate_source": f"{sms} SMs x 128 FP32 FMA lanes per SM per clock x {sm_mhz:.0f} MHz "
+                                        "(median SM clock sampled during the timed region)"})
     # the same 512-byte-row gather alone, over a slab as large as the widest step's state tile
     ceiling = gather_ceiling(dev, max(cone.rows_len))
     roofline.update({"l2_gather_ceiling_gbs": round(ceiling, 1),
@@ -721,7 +733,7 @@ def main():
                                        f"{inst.e:,} synapses), 6-step light-cone forward, float16 deviation",
                            "positions_per_gpu": B, "global_positions": B * world, "l2": "inputs larger than L2",
                            "parallelism": f"positions sharded over {world} GPU(s), wiring replicated, no collective"},
-                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks.summary(),
+                "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clk,
                 "gpu_launches": args.steps * (STEPS_T + 1),
                 "weight_version_ms": round(weight_version_ms, 3),
                 "light_cone": {"rows": cone.rows_len, "nnz": cone.nnz, "edge_visits": cone.edge_visits}}

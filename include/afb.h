@@ -179,19 +179,35 @@ AFB_API int afb_graph_forward(const afb_graph *graph, const float *w, const floa
                       float h_max, const float *u, int64_t ld_u, int64_t batch, int steps, float *h,
                       int64_t ld_h, void *workspace, size_t workspace_bytes, void *stream);
 
-/* ---- policy head: legal-move logits only (chessfly/model.py:104 + 124-126) --------------------------
- * The reference evaluates the dense policy logits (B, N_MOVES) = r W^T + b + F[:, move_from] + T[:, move_to]
- * and then gathers logits[rows, cols] of the legal moves.  This entry point computes only the m gathered
- * entries:  out[i] = r[rows[i]] . w[cols[i]] + b[cols[i]] + f[rows[i], move_from[cols[i]]]
- *                                                         + t[rows[i], move_to[cols[i]]]
- * r (batch, n_out) and w (n_moves, n_out) row-major float32; b (n_moves); f, t (batch, n_sq) row-major
- * (the factorised from/to terms, already multiplied out); move_from, move_to (n_moves) int64 in [0, n_sq).
- * rows in [0, batch) and cols in [0, n_moves) as int64; an index out of range gives NaN for that entry.
- * One warp per entry; asynchronous on `stream`. */
-AFB_API int afb_legal_logits(int64_t m, const int64_t *rows, const int64_t *cols, int64_t batch, int64_t n_out,
-                             const float *r, int64_t n_moves, const float *w, const float *b, int64_t n_sq,
-                             const float *f, const float *t, const int64_t *move_from, const int64_t *move_to,
-                             float *out, void *stream);
+/* ---- the readout heads on the tensor cores (chessfly/model.py:103-105) -----------------------------
+ * The reference normalises the output neurons with RunningNorm and applies the dense heads in float32:
+ *     r = clamp((out^T - mean) / sqrt(var + eps), -clip, clip)
+ *     logits = r Wp^T + bp + (r Wf^T + bf)[:, move_from] + (r Wt^T + bt)[:, move_to],  wdl = r Wv^T + bv.
+ * The from/to terms are linear in r, so the caller folds them into the policy rows once per weight version
+ * (W[m] = Wp[m] + Wf[move_from[m]] + Wt[move_to[m]], b[m] likewise) and stacks the value rows below:
+ * W (n_rows x n_out) with n_rows = n_policy + n_value.
+ *
+ * afb_heads_split: hi = fp16(x), lo = fp16((x - hi) * 2^11) of a float32 matrix src (rows x cols, row
+ *   stride ld_src) into hi, lo (rows x ld_dst float16, columns cols..ld_dst-1 zero).  Run once per weight
+ *   version on W.  Asynchronous on `stream`.
+ * afb_readout_workspace: bytes of scratch afb_readout_heads needs for `batch` positions.
+ * afb_readout_heads: out (n_out, batch) float32 with row stride ld_r (the layout of the light-cone
+ *   forward's output); mean, var (n_out) the normaliser's statistics; w_hi, w_lo from afb_heads_split
+ *   (row stride ldw, a multiple of 8; 16-byte aligned); bias (n_rows) float32.  Writes
+ *   logits[p * ld_logits + m] for m < n_policy (float32, or float16 with logits_f16 != 0) and
+ *   values[p * ld_values + j] = D[n_policy + j, p] for j < n_rows - n_policy, p < batch.  The product runs
+ *   on the tensor cores with both operands split into float16 hi and lo parts and two float32
+ *   accumulators (D = W_hi r_hi + (W_hi r_lo + W_lo r_hi) / 2^11): float32 accuracy (~1e-6 relative).
+ *   status: optional device int, OR-ed with a non-zero code if one of the kernel's bounded waits gave up
+ *   (never expected).  Asynchronous on `stream`. */
+AFB_API int afb_heads_split(int64_t rows, int64_t cols, const float *src, int64_t ld_src, void *hi, void *lo,
+                            int64_t ld_dst, void *stream);
+AFB_API size_t afb_readout_workspace(int64_t batch, int64_t n_out);
+AFB_API int afb_readout_heads(int64_t n_out, int64_t batch, const float *out, int64_t ld_r, const float *mean,
+                              const float *var, float eps, float clip, int64_t n_rows, int64_t n_policy, const void *w_hi,
+                              const void *w_lo, int64_t ldw, const float *bias, void *logits, int64_t ld_logits,
+                              int logits_f16, float *values, int64_t ld_values, void *workspace, size_t workspace_bytes,
+                              int *status, void *stream);
 
 /* ---- the float16 input map (chessfly/model.py:101-102) ----------------------------------------------
  * The reference computes the drive of the input neurons as  u_in = (x[:, :k] W^T + b) * input_gain,

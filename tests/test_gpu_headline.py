@@ -4,9 +4,11 @@ GPU, the bench's exact drive) and configuration 5 (training, B = 2,048).
 - The float16 deviation path at B = 35,840 against the oracle in float64 on 72 columns taken from the start,
   the middle and the end of the batch (north-star gate: 2e-3 relative L2), and the float32 path at the same
   batch on the same columns (1e-4), plus float16 against float32 over the whole batch.
-- The policy argmax gate through the real FlyChessNet (RunningNorm + the dense heads) on 2,240 positions:
-  float16 inference against float32 inference of the same network (>= 99.5% agreement, logits within 2e-3
-  relative L2).  The float32 network is pinned to the reference's own run by test_gpu_model.
+- The policy argmax gate through the real FlyChessNet (RunningNorm + heads) on 2,240 positions: float16
+  inference (deviation path + the tensor-core readout) against the float32 network with the reference's
+  float32 head layers (>= 99.5% agreement, logits within 2e-3 relative L2), and the tensor-core readout on
+  the float32 recurrence within 1e-5 of those layers.  The float32 network is pinned to the reference's own
+  run by test_gpu_model.
 - Configuration 5's backward at B = 2,048: the loss weights 16 positions spread over all 16 batch tiles of
   the SDDMM partial sums, and every gradient is compared with the oracle's float64 backward of those 16
   positions (1e-4); the whole-batch gradient equals the sum of its four 512-position quarters.
@@ -106,11 +108,14 @@ def test_flychessnet_float16_policy_agrees_with_float32_on_the_full_graph(full):
     net.eval()
     x = torch.from_numpy(synth.boards(2240, seed=32)).to(DEV)
     with torch.no_grad():
-        l32, v32 = net(x)
+        l32, v32 = net.dense_heads(net.readout(x))            # float32 throughout, the reference's layers
+        l32_tc, v32_tc = net(x)                                # float32 recurrence, tensor-core readout
         net.infer_dtype = torch.float16
-        l16, v16 = net(x)
+        l16, v16 = net(x)                                      # the self-play path
     assert l16.dtype == torch.float32 and l16.shape == (2240, 4168)
-    l32, l16 = l32.cpu().numpy(), l16.cpu().numpy()
+    l32, l16, l32_tc = l32.cpu().numpy(), l16.cpu().numpy(), l32_tc.cpu().numpy()
+    assert orc.rel_l2(l32_tc, l32) < 1e-5, orc.rel_l2(l32_tc, l32)
+    assert orc.rel_l2(v32_tc.cpu().numpy(), v32.cpu().numpy()) < 1e-5
     assert orc.rel_l2(l16, l32) < F16_GATE, orc.rel_l2(l16, l32)
     agree = float((l16.argmax(1) == l32.argmax(1)).mean())
     assert agree >= 0.995, agree

@@ -81,10 +81,11 @@ def test_train_step_matches_reference():
 
 
 def _plain(net, x, rows, cols):
-    """The reference's Evaluator.submit + result (chessfly/model.py:120-132), eager."""
+    """The reference's Evaluator.submit + result (chessfly/model.py:120-132), eager, with its float32 head
+    layers (``dense_heads``)."""
     net.eval()
     with torch.no_grad():
-        logits, wdl = net(torch.from_numpy(x).to(DEV).float())
+        logits, wdl = net.dense_heads(net.readout(torch.from_numpy(x).to(DEV).float()))
         v = net.expected_value(wdl.float()).cpu().numpy()
         if rows is None:
             return logits.half().cpu().numpy(), v
@@ -163,33 +164,64 @@ def test_two_rounds_in_flight_and_weight_updates_between_rounds(small_net):
             small_net.policy.bias.sub_(1.0)
 
 
-def test_legal_logits_kernel_against_torch():
-    """afb_legal_logits at the real head sizes (2,333 outputs, 4,168 moves, 64 squares) against the dense
-    product and gather in float64; an out-of-range index gives NaN for its entry only."""
+@pytest.mark.parametrize("batch", [1, 37, 300, 1120])
+def test_readout_heads_kernel_against_float64(batch):
+    """afb_readout_heads (RunningNorm + folded heads on the tensor cores, split float16 operands) at the real
+    head sizes (2,333 output neurons, 4,168 policy rows + 3 value rows) against the normaliser and the
+    dense product in float64; some entries are beyond the clip.  float32 accuracy is the bar (1e-5; the
+    split is ~1e-6), and the float16 output is that result rounded once."""
     from alphafly_b200 import _lib
-    from alphafly_b200.encoding import move_squares
-    g = torch.Generator(device=DEV).manual_seed(0)
-    batch, o = 64, 2333
-    r = torch.randn(batch, o, device=DEV, generator=g)
-    w = torch.randn(4168, o, device=DEV, generator=g) / o ** 0.5
-    b = torch.randn(4168, device=DEV, generator=g)
-    f = torch.randn(batch, 64, device=DEV, generator=g)
-    t = torch.randn(batch, 64, device=DEV, generator=g)
-    frm, to = (torch.as_tensor(a, device=DEV) for a in move_squares())
-    rows = torch.randint(0, batch, (5000,), device=DEV, generator=g)
-    cols = torch.randint(0, 4168, (5000,), device=DEV, generator=g)
-    rows[17], cols[18] = batch, -1                       # out of range
-    out = torch.empty(5000, device=DEV)
+    g = torch.Generator(device=DEV).manual_seed(batch)
+    o, n_pol, n_val = 2333, 4168, 3
+    rows = n_pol + n_val
+    out = 4.0 + torch.randn(o, batch, device=DEV, generator=g) * 0.3        # the forward's (n_out, batch) layout
+    mean = 4.0 + torch.randn(o, device=DEV, generator=g) * 0.05
+    var = (torch.rand(o, device=DEV, generator=g) * 0.1 + 0.005) ** 2           # small: many clip at +-8
+    w = torch.randn(rows, o, device=DEV, generator=g) / o ** 0.5
+    bias = torch.randn(rows, device=DEV, generator=g)
+    ldw = -(-o // 8) * 8
+    hi = torch.empty(rows, ldw, dtype=torch.float16, device=DEV)
+    lo = torch.empty_like(hi)
     lib = _lib.load()
-    _lib.check(lib.afb_legal_logits(5000, rows.data_ptr(), cols.data_ptr(), batch, o, r.data_ptr(), 4168, w.data_ptr(),
-                                    b.data_ptr(), 64, f.data_ptr(), t.data_ptr(), frm.data_ptr(), to.data_ptr(),
-                                    out.data_ptr(), torch.cuda.current_stream().cuda_stream))
-    dense = (r.double() @ w.double().T + b.double() + f.double()[:, frm] + t.double()[:, to])
-    ok = torch.ones(5000, dtype=torch.bool, device=DEV)
-    ok[17] = ok[18] = False
-    ref = dense[rows[ok], cols[ok]]
-    assert torch.isnan(out[17]) and torch.isnan(out[18])
-    assert float((out[ok].double() - ref).abs().max()) < 1e-4
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.afb_heads_split(rows, o, w.data_ptr(), o, hi.data_ptr(), lo.data_ptr(), ldw, stream))
+    ws = torch.empty(lib.afb_readout_workspace(batch, o), dtype=torch.uint8, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    res = {}
+    for f16 in (0, 1):
+        logits = torch.full((batch, n_pol), float("nan"), dtype=torch.float16 if f16 else torch.float32, device=DEV)
+        values = torch.full((batch, n_val), float("nan"), device=DEV)
+        _lib.check(lib.afb_readout_heads(o, batch, out.data_ptr(), out.stride(0), mean.data_ptr(), var.data_ptr(), 1e-8, 8.0,
+                                         rows, n_pol, hi.data_ptr(), lo.data_ptr(), ldw, bias.data_ptr(), logits.data_ptr(),
+                                         n_pol, f16, values.data_ptr(), n_val, ws.data_ptr(), ws.numel(), status.data_ptr(),
+                                         stream))
+        res[f16] = (logits, values)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    r = ((out.double().T - mean.double()) / (var.double() + 1e-8).sqrt()).clamp(-8, 8)
+    assert float((r.abs() == 8).double().mean()) > 0.01                        # the clip is exercised
+    dense = r @ w.double().T + bias.double()
+    logits, values = res[0]
+    assert torch.isfinite(logits).all() and torch.isfinite(values).all()
+    err = float((logits.double() - dense[:, :n_pol]).norm() / dense[:, :n_pol].norm())
+    verr = float((values.double() - dense[:, n_pol:]).norm() / dense[:, n_pol:].norm())
+    assert err < 1e-5 and verr < 1e-5, (err, verr)
+    torch.testing.assert_close(res[1][0], logits.half(), rtol=0, atol=0)          # one rounding of the same sums
+    torch.testing.assert_close(res[1][1], values, rtol=0, atol=0)
+
+
+def test_folded_heads_equal_the_factorised_heads(small_net):
+    """FlyChessNet.forward in inference (the tensor-core readout with the from/to terms folded into the
+    policy rows) against the float32 layers of the reference's forward on the same normalised state."""
+    net = small_net.eval()
+    x = torch.from_numpy(synth.boards(300, seed=12)).to(DEV)
+    with torch.no_grad():
+        net.infer_dtype = torch.float32
+        logits, wdl = net(x)
+        ref, ref_wdl = net.dense_heads(net.readout(x))
+        net.infer_dtype = torch.float16
+    assert orc.rel_l2(logits.cpu().numpy(), ref.cpu().numpy()) < 1e-5
+    assert orc.rel_l2(wdl.cpu().numpy(), ref_wdl.cpu().numpy()) < 1e-5
 
 
 def _padded_half(a: torch.Tensor) -> torch.Tensor:
