@@ -531,7 +531,10 @@ __global__ void __launch_bounds__(kWarps * 32, kRingMinBlocks) step_kernel_ring(
 // ---- register kernel (default) --------------------------------------------------------------------
 // Row by row, one warp per 512-byte row tile, kChunk gathered rows in flight per lane in registers; a
 // chunk never straddles a row, so the gathered registers are dead when a row's epilogue runs.  The
-// column indices and values of 32 edges are loaded coalesced and broadcast with shuffles.  Measured on
+// column indices and values of 32 edges are loaded coalesced and broadcast with shuffles.  A gather's
+// address is the tile's slab base (the same for the whole CTA) plus a 32-bit byte offset, which keeps
+// the per-lane address state to one register (measured 150 vs 154 ms per configuration-3 forward
+// against 64-bit per-lane pointers).  Measured on
 // the configuration-3 workload: the gather's throughput grows with the warps per SM, and a spill in the
 // loop costs more than any occupancy gains, so the tuned point is kChunk = 4 at 5 CTAs per SM (48
 // registers, no spills).
@@ -586,7 +589,9 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks) step_kernel(const Ste
 
     const int tile = blockIdx.x / a.n_items;
     const int off = lane * V;
-    const T *x_tile = static_cast<const T *>(a.x_in) + (int64_t)tile * a.ts_in + off;
+    // uniform base of this tile's slab + a 32-bit per-lane byte offset (a slab is far below 4 GB)
+    const char *x_base = reinterpret_cast<const char *>(static_cast<const T *>(a.x_in) + (int64_t)tile * a.ts_in);
+    const uint32_t lane_b = (uint32_t)lane * 16u;
     const LeanWarp &me = s_w[warp];
     for (int i = vld(me.is); i <= vld(me.ilast); ++i) {
         int eb, ee;
@@ -617,7 +622,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks) step_kernel(const Ste
                 uint4 x[kChunkR];
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u)
-                    x[u] = __ldg(reinterpret_cast<const uint4 *>(x_tile + __shfl_sync(kFull, my_col, k + u) * BT));
+                    x[u] = __ldg(reinterpret_cast<const uint4 *>(x_base + ((uint32_t)__shfl_sync(kFull, my_col, k + u) * 512u + lane_b)));
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) G::fma(acc, __shfl_sync(kFull, my_val, k + u), x[u]);
             }
@@ -627,7 +632,7 @@ __global__ void __launch_bounds__(kWarps * 32, kMinBlocks) step_kernel(const Ste
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) {
                     const int c = __shfl_sync(kFull, my_col, (k + u) & 31);
-                    x[u] = k + u >= n ? make_uint4(0, 0, 0, 0) : __ldg(reinterpret_cast<const uint4 *>(x_tile + c * BT));
+                    x[u] = k + u >= n ? make_uint4(0, 0, 0, 0) : __ldg(reinterpret_cast<const uint4 *>(x_base + ((uint32_t)c * 512u + lane_b)));
                 }
 #pragma unroll
                 for (int u = 0; u < kChunkR; ++u) G::fma(acc, __shfl_sync(kFull, my_val, (k + u) & 31), x[u]);
@@ -709,6 +714,8 @@ void launch(const StepArgs &args, cudaStream_t s) {
         }
         step_kernel_ring<T, TV><<<(unsigned)blocks, kWarps * 32, kRingBytes, s>>>(a);
     } else {
+        // the register kernel addresses a tile's slab with 32-bit byte offsets
+        AFB_CHECK(a.ts_in * (int64_t)sizeof(T) <= (int64_t)UINT32_MAX, "a step's state tile exceeds 4 GB");
         step_kernel<T, TV><<<(unsigned)blocks, kWarps * 32, 0, s>>>(a);
     }
     AFB_LAUNCHED();
