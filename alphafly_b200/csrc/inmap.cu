@@ -22,7 +22,8 @@
 //     stores, so the global writes are whole lines; a u whose rows do not start on 16 bytes takes scalar
 //     stores.
 // Every mbarrier wait is bounded: a wait that gives up sets *status (the host reads it) and the CTA
-// skips ahead instead of hanging; TMEM is always released.  No cluster, no multicast.
+// skips ahead instead of hanging; TMEM is always released.  No thread-block clusters: every TMA load fills
+// this CTA's own shared memory.
 #include <cstring>
 
 #include "tc.cuh"

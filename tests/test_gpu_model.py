@@ -317,6 +317,7 @@ def test_sharded_evaluator_equals_one_evaluator(small_net, lazy):
     rows, cols = rows[perm], cols[perm]
     one = Evaluator(small_net, DEV)
     many = ShardedEvaluator(small_net, devices)
+    assert [str(r.brain.pre.device) for r in many.replicas] == devices      # two GPUs: one replica on each
     req = (x, None, None) if lazy else (x, rows, cols)
     a, b = one(*req), many(*req)
     assert a[0].shape == b[0].shape and a[0].dtype == b[0].dtype
