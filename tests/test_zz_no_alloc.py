@@ -119,7 +119,8 @@ def test_noalloc_forward_on_a_second_device_and_device_checks():
                                                 out.stride(0), s1))
         torch.cuda.synchronize(dev1)
         assert orc.rel_l2(out.cpu().numpy(), ref.cpu().numpy()) < 1e-6
-        s0 = ctypes.c_void_p(torch.cuda.current_stream(torch.device("cuda", 0)).cuda_stream)
+        other = torch.cuda.Stream(device=torch.device("cuda", 0))          # a created stream: the legacy default
+        s0 = ctypes.c_void_p(other.cuda_stream)                            # stream's handle names no device
         rc = lib.afb_cone_forward_noalloc(cone._h, _lib.MODE_DEV16, _ptr(u), u.stride(0), u.shape[1], _ptr(out),
                                           out.stride(0), s0)
         assert rc == _lib.EINVAL and b"stream belongs to device 0" in lib.afb_last_error()
