@@ -633,8 +633,8 @@ def main():
                 "traffic": measured_traffic() if B == 35_840 else None,
                 "traffic_source": "profiles/step_kernel_traffic_config3.txt: ncu DRAM bytes of the 6 step launches at "
                                   "B = 2,048 (8 batch tiles), scaled by 17.5 to the 140 tiles of B = 35,840; per launch",
-                "kernel": "step_kernel<__half,__half> (steps 3-6) and step_kernel_ring<__half,__half> (steps 1-2): "
-                          "6 launches per forward",
+                "kernel": "step_kernel<__half,__half> (steps 3-6), step_kernel_pair<__half,__half> (step 2) and "
+                          "step_kernel_nosyn<__half> (step 1): 6 launches per forward",
                 "algorithmic_bytes_per_launch": int(sum(per_step_bytes) / STEPS_T),
                 "launch_ms": [round(x, 3) for x in kernel_ms],
                 "l2_gather_bytes_per_forward": int(gathered),
