@@ -434,9 +434,9 @@ __global__ void __launch_bounds__(kWarps * 32, kPairMinBlocks) step_kernel_pair(
                     G::fma(acc_b, v, xb[u]);
                 }
             }
-            if (n_full < n) {                                 // the window's last, single synapse
-                const uint32_t o = (uint32_t)__shfl_sync(kFull, my_col, n_full) * 512u + lane_b;
-                const uint32_t v = __shfl_sync(kFull, my_val, n_full);
+            for (int k = n_full; k < n; ++k) {               // the window's last synapses, one at a time
+                const uint32_t o = (uint32_t)__shfl_sync(kFull, my_col, k) * 512u + lane_b;
+                const uint32_t v = __shfl_sync(kFull, my_val, k);
                 const uint4 xa = __ldg(reinterpret_cast<const uint4 *>(base_a + o));
                 const uint4 xb = __ldg(reinterpret_cast<const uint4 *>(base_b + o));
                 G::fma(acc_a, v, xa);
