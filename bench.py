@@ -290,12 +290,17 @@ def reference_arm(args, rank, world):
 
 def probe_arm(args):
     """Gather ceiling of the step kernel's load path (include/afb_probe.h) on configuration 3's widest slab,
-    against warps per SM."""
+    against warps per SM, then against the slab's size."""
     dev = torch.device("cuda", 0)
     rows = 166_688
     for bps in (2, 3, 4, 5, 6, 8):
         print(json.dumps({"probe": "ldg 16 B per lane, 8 rows in flight", "warps_per_sm": 8 * bps, "slab_rows": rows,
                           "gbs": round(gather_ceiling(dev, rows, blocks_per_sm=bps), 1)}), flush=True)
+    # the slab against the L2: 12 MB .. 164 MB at the step kernel's 40 warps per SM and at 64
+    for sr in (24_000, 48_000, 72_000, 96_000, 120_000, 144_000, 166_688, 200_000, 240_000, 320_000):
+        print(json.dumps({"probe": "ldg 16 B per lane, 8 rows in flight", "slab_rows": sr, "slab_mb": round(sr * 512 / 1e6, 1),
+                          "gbs_40_warps": round(gather_ceiling(dev, sr, blocks_per_sm=5), 1),
+                          "gbs_64_warps": round(gather_ceiling(dev, sr, blocks_per_sm=8), 1)}), flush=True)
 
 
 def inmap_arm(args):
