@@ -58,6 +58,8 @@ SIGNATURES = {
     "afb_readout_workspace": (_sz, [_i64, _i64]),
     "afb_readout_heads": (_int, [_i64, _i64, _p, _i64, _p, _p, _f, _f, _i64, _i64, _p, _p, _i64, _p, _p, _i64, _int, _p,
                                  _i64, _p, _sz, _p, _p]),
+    "afb_gemm_workspace": (_sz, [_i64, _i64, _i64]),
+    "afb_gemm_f32": (_int, [_i64, _i64, _i64, _f, _p, _i64, _int, _p, _i64, _int, _p, _int, _f, _p, _i64, _p, _sz, _p, _p]),
 }
 
 # the entry points of include/afb_probe.h (libafb_probe.so)

@@ -149,6 +149,7 @@ class LightCone:
         self.n_in, self.n_out = in_idx.numel(), out_idx.numel()
         self.n = rnn.n
         self._weights: dict[int, tuple] = {}
+        self.generation = {}                  # mode -> count of set_weight_tensors calls (which constants are live)
 
     def _export(self, field: str, t: int, size: int) -> torch.Tensor:
         out = torch.empty(int(size), dtype=torch.long, device=self.device)
@@ -179,6 +180,7 @@ class LightCone:
     def set_weight_tensors(self, mode: int, w, bias, alpha_logit, h_max) -> None:
         """Constants of ``mode`` from explicit edge weights, bias and alpha logits (``afb_cone_set_weights``)."""
         self._weights.pop(mode, None)
+        self.generation[mode] = self.generation.get(mode, 0) + 1
         with torch.cuda.device(self.device):
             w = w.detach().float().contiguous()
             bias = bias.detach().float().contiguous()
@@ -303,6 +305,7 @@ class _ConeTrain(torch.autograd.Function):
             _lib.check(lib.afb_cone_forward_train(cone._h, _ptr(u_in), u_in.stride(0), batch, _ptr(out), batch,
                                                   _ptr(saved), saved_bytes, _stream(dev)))
         ctx.cone, ctx.h_max, ctx.batch, ctx.n_in, ctx.saved_state = cone, h_max, batch, u_in.shape[0], saved
+        ctx.generation = cone.generation[_lib.MODE_F32]
         ctx.save_for_backward(w.detach(), bias.detach(), alpha_logit.detach())
         return out
 
@@ -312,8 +315,9 @@ class _ConeTrain(torch.autograd.Function):
         w, bias, alpha_logit = ctx.saved_tensors
         dev = cone.device
         lib = cone._lib
-        # the cone's constants must be those of this forward's weights
-        cone.set_weight_tensors(_lib.MODE_F32, w, bias, alpha_logit, ctx.h_max)
+        # the cone's constants must be those of this forward's weights: set again if another call replaced them
+        if cone.generation.get(_lib.MODE_F32) != ctx.generation:
+            cone.set_weight_tensors(_lib.MODE_F32, w, bias, alpha_logit, ctx.h_max)
         g_out = g_out.float().contiguous()
         with torch.cuda.device(dev):
             ws_bytes = lib.afb_cone_backward_workspace(cone._h, batch)

@@ -22,12 +22,12 @@ from collections import OrderedDict
 import numpy as np
 import torch
 from torch import nn
-from torch.nn import functional as F
 
 from . import _lib
 from .brain import ConnectomeRNN
 from .connectome import Connectome
 from .encoding import N_BASE, N_FEATURES, N_MOVES, move_squares
+from .gemm import affine
 
 READOUT_SUPERCLASSES = ("descending_neuron",)   # plus every efferent neuron (chessfly/model.py:23)
 
@@ -113,7 +113,10 @@ class FlyChessNet(nn.Module):
             w16, b16 = self.half_encoder()
             return input_map_f16(w16, b16, x[:, :k], g, self._map_status(x.device))
         w, b = self.encoder.weight[:, :k], self.encoder.bias
-        u = torch.addmm(b.unsqueeze(1), w, x[:, :k].float().T, beta=g, alpha=g)
+        if x.is_cuda and torch.is_grad_enabled():      # training: the product on the tensor cores, float32-accurate
+            u = affine(w, x[:, :k].float(), b, 1, alpha=g, beta=g)
+        else:
+            u = torch.addmm(b.unsqueeze(1), w, x[:, :k].float().T, beta=g, alpha=g)
         return u.to(dtype).contiguous()
 
     @torch.no_grad()
@@ -167,10 +170,17 @@ class FlyChessNet(nn.Module):
         """The heads as the reference's float32 layers on the normalised state r (B, len(out_idx))
         (chessfly/model.py:104-105); the training path, through which autograd runs.  The from/to terms
         F[:, move_from[m]] + T[:, move_to[m]] are taken as [F, T] @ move_select, the same sums (each column
-        of move_select holds two ones)."""
-        ft = F.linear(r, torch.cat([self.policy_from.weight, self.policy_to.weight]),
-                      torch.cat([self.policy_from.bias, self.policy_to.bias]))
-        logits = torch.addmm(self.policy(r), ft, self.move_select)
+        of move_select holds two ones).  In training (autograd on, CUDA) the policy and from/to products and
+        their gradients run on the tensor cores at float32 accuracy (``gemm.affine``, libafb's afb_gemm_f32)."""
+        w_ft = torch.cat([self.policy_from.weight, self.policy_to.weight])
+        b_ft = torch.cat([self.policy_from.bias, self.policy_to.bias])
+        if r.is_cuda and torch.is_grad_enabled():
+            policy = affine(r, self.policy.weight, self.policy.bias, 2)
+            ft = affine(r, w_ft, b_ft, 2)
+        else:
+            policy = self.policy(r)
+            ft = torch.addmm(b_ft, r, w_ft.T)
+        logits = torch.addmm(policy, ft, self.move_select)
         return logits, self.value(r)
 
     @torch.no_grad()

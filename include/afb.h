@@ -221,6 +221,22 @@ AFB_API int afb_readout_heads(int64_t n_out, int64_t batch, const float *out, in
 AFB_API int afb_input_map_f16(int64_t n_in, int64_t batch, int64_t k_dim, const void *w, int64_t ldw, const void *x,
                               int64_t ldx, const void *b, float gain, void *u, int64_t ldu, int *status, void *stream);
 
+/* ---- float32 GEMMs of the training path (chessfly/model.py:95-105 trained by chessfly/train.py:126-138) --
+ * The reference trains its encoder and heads as float32 nn.Linear layers (their forward and the two
+ * gradient products of each).  afb_gemm_f32 computes
+ *     r[i * ld_r + j] = alpha * sum_{l < k} X[i, l] Y[j, l] + beta * bias        (i < p, j < q)
+ * with X[i, l] = x[i * ld_x + l] (x_trans = 0) or x[l * ld_x + i] (x_trans = 1), Y likewise, and bias = 0
+ * (bias_dim 0), bias[i] (1) or bias[j] (2).  float32 in and out, float32 accuracy (~1e-6 relative to the
+ * largest products): each operand is scaled by a power of two and split into float16 hi and lo parts, the
+ * products run on the tensor cores (tcgen05.mma) with two float32 accumulators.  workspace: at least
+ * afb_gemm_workspace(p, q, k) bytes; one call at a time per workspace.  status: optional device int, OR-ed
+ * with a non-zero code if one of the kernel's bounded waits gave up (never expected).  Asynchronous on
+ * `stream`. */
+AFB_API size_t afb_gemm_workspace(int64_t p, int64_t q, int64_t k);
+AFB_API int afb_gemm_f32(int64_t p, int64_t q, int64_t k, float alpha, const float *x, int64_t ld_x, int x_trans,
+                         const float *y, int64_t ld_y, int y_trans, const float *bias, int bias_dim, float beta, float *r,
+                         int64_t ld_r, void *workspace, size_t workspace_bytes, int *status, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
