@@ -60,7 +60,8 @@ class RunningNorm(nn.Module):
     def forward(self, r: torch.Tensor) -> torch.Tensor:
         if self.training and r.shape[0] > 1:
             with torch.no_grad():
-                m = 1.0 if not self.initialised else self.momentum
+                # weight 1 for the first batch, else momentum; chosen on the device (no host read-back)
+                m = torch.where(self.initialised, self.momentum, 1.0).to(self.mean.dtype)
                 mean, var = self.batch_sync(r) if self.batch_sync is not None else (r.mean(0), r.var(0))
                 self.mean.lerp_(mean, m)
                 self.var.lerp_(var, m)
