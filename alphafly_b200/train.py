@@ -265,7 +265,9 @@ class BucketedAllReduce:
             work.wait()
             params = self.buckets[k]
             n = sum(p.numel() for p in params)
-            present = flat[n:].tolist()
+            # the presence flags are read (a host synchronisation) only for a bucket in which this rank
+            # has a parameter without a gradient: the others take the mean whatever the flags say
+            present = flat[n:].tolist() if any(p.grad is None for p in params) else [1.0] * len(params)
             flat = flat[:n] / world
             at = 0
             for p, seen in zip(params, present):
