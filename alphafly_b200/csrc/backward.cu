@@ -202,12 +202,14 @@ __global__ void __launch_bounds__(256, 5) bwd_spmm_t(int n_cols, const int *__re
     *reinterpret_cast<float4 *>(gh_prev + tile * ts_prev + (int64_t)j * bt + off) = acc;
 }
 
-__global__ void bwd_edge_sum(int64_t nnz, int64_t tiles, const float *__restrict__ part, const int *__restrict__ t_order,
-                             const int *__restrict__ edges, float *__restrict__ g_w) {
+// dL/dw of the step: the per-tile partials of each transpose position summed in tile order (deterministic),
+// added at that synapse's edge of W (t_edges = edges[t_order], one gather instead of two dependent ones).
+__global__ void bwd_edge_sum(int64_t nnz, int64_t tiles, const float *__restrict__ part, const int *__restrict__ t_edges,
+                             float *__restrict__ g_w) {
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < nnz; e += (int64_t)gridDim.x * blockDim.x) {
         float s = 0.f;
         for (int64_t t = 0; t < tiles; ++t) s += part[t * nnz + e];
-        g_w[edges[t_order[e]]] += s;
+        g_w[t_edges[e]] += s;
     }
 }
 
@@ -422,7 +424,7 @@ int afb_cone_backward(const afb_cone *c, const float *g_out, int64_t ld_g, int64
                                                   part, m.nnz);
                 AFB_LAUNCHED();
                 if (m.nnz) {
-                    bwd_edge_sum<<<grid_for(m.nnz, kBlock), kBlock, 0, s>>>(m.nnz, tiles, part, m.t_order.get(), m.edges.get(), g_w);
+                    bwd_edge_sum<<<grid_for(m.nnz, kBlock), kBlock, 0, s>>>(m.nnz, tiles, part, m.t_edges.get(), g_w);
                     AFB_LAUNCHED();
                 }
             }

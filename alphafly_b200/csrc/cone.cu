@@ -365,6 +365,7 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
             m.col.alloc(nnz);
             m.t_col.alloc(nnz);
             m.t_order.alloc(nnz);
+            m.t_edges.alloc(nnz);
             if (nnz) {
                 DevBuf<long long> key(nnz), key_sorted(nnz);
                 DevBuf<int> iota(nnz);
@@ -379,6 +380,7 @@ int afb_cone_create(afb_cone **out, int64_t n, int64_t e, const int64_t *pre, co
                 AFB_CUDA(cub::DeviceRadixSort::SortPairs(tmp.need(bytes), bytes, key.get(), key_sorted.get(), iota.get(),
                                                          m.t_order.get(), (int)nnz, 0, end_bit, s));
                 gather_int<<<grid_for(nnz, kBlock), kBlock, 0, s>>>(m.post.get(), m.t_order.get(), m.t_col.get(), (int)nnz);
+                gather_int<<<grid_for(nnz, kBlock), kBlock, 0, s>>>(m.edges.get(), m.t_order.get(), m.t_edges.get(), (int)nnz);
                 AFB_LAUNCHED();
             }
             crow_from_rows(m.post.get(), nnz, nr, m.crow, tmp, s);

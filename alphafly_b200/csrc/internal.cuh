@@ -35,6 +35,7 @@ struct Csr {
     DevBuf<int> crow, col;         // crow (n_rows + 1), col (nnz): local column index
     DevBuf<int> edges, post;       // edges (nnz): index into W's edge list; post (nnz): local row
     DevBuf<int> t_crow, t_col, t_order;  // CSR of the transpose, and the edge permutation into it
+    DevBuf<int> t_edges;           // (nnz) edges[t_order]: W's edge index at each position of the transpose
     DevBuf<int> t_heavy;           // (n_cols) rows of the transpose, longest first (backward launch order)
     // schedule of items of ~kItemCost, and of ~kFineItemCost for launches whose kItemCost items would be
     // too few CTAs to fill the GPU (narrow batches on small graphs or small light-cone steps)
