@@ -185,8 +185,11 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_kernel(const __grid_constant
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
             const uint32_t y_hi = tiles + s * kStageBytes, y_lo = y_hi + kTileBytes, x_hi = y_hi + 2 * kTileBytes,
                            x_lo = y_hi + 3 * kTileBytes;
+            // the last k block takes only the 16-wide steps that hold data; the others would multiply zero fill
+            const int nj = min(kBK / kMmaK, (k_dim - kb * kBK + kMmaK - 1) / kMmaK);
 #pragma unroll
             for (int j = 0; j < kBK / kMmaK; ++j) {
+                if (j >= nj) break;
                 const uint32_t off = j * kMmaK * 2;
                 const uint32_t first = (kb > 0 || j > 0) ? 1u : 0u;
                 tc::mma_f16(tmem, smem_desc(y_hi + off), smem_desc(x_hi + off), kIdesc, first);

@@ -204,9 +204,13 @@ __global__ void __launch_bounds__(kThreads, 1) input_map_kernel(const __grid_con
                 }
                 asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
                 const uint32_t a_src = ring + s * kStageBytes, b_src = a_src + kOperandBytes;
+                // the last k block takes only the 16-wide steps that hold features (K = 838: 1 of 4); the
+                // skipped steps would multiply TMA's zero fill, so the sums are the same
+                const int nj = min(kBK / kMmaK, (k_dim - kb * kBK + kMmaK - 1) / kMmaK);
 #pragma unroll
                 for (int j = 0; j < kBK / kMmaK; ++j)
-                    mma_pair(d, smem_desc(a_src + j * kMmaK * 2), smem_desc(b_src + j * kMmaK * 2), (kb > 0 || j > 0) ? 1u : 0u);
+                    if (j < nj)
+                        mma_pair(d, smem_desc(a_src + j * kMmaK * 2), smem_desc(b_src + j * kMmaK * 2), (kb > 0 || j > 0) ? 1u : 0u);
                 commit_pair(empty(s));                                   // the stage is free in both CTAs once
                 commit_pair(map_to(empty(s), 1));                        // these MMAs have read it
             }

@@ -170,8 +170,11 @@ __global__ void __launch_bounds__(kThreads, 1) readout_heads_kernel(const __grid
             asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory");
             const uint32_t w_hi = tiles + s * kStageBytes, w_lo = w_hi + kTileBytes, r_hi = w_hi + 2 * kTileBytes,
                            r_lo = w_hi + 3 * kTileBytes;
+            // the last k block takes only the 16-wide steps that hold data; the others would multiply zero fill
+            const int nj = min(kBK / kMmaK, (k_dim - kb * kBK + kMmaK - 1) / kMmaK);
 #pragma unroll
             for (int j = 0; j < kBK / kMmaK; ++j) {
+                if (j >= nj) break;
                 const uint32_t off = j * kMmaK * 2;
                 const uint32_t first = (kb > 0 || j > 0) ? 1u : 0u;
                 tc::mma_f16(tmem, smem_desc(w_hi + off), smem_desc(r_hi + off), kIdesc, first);
