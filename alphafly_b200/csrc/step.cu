@@ -480,6 +480,130 @@ __global__ void __launch_bounds__(kWarps * 32, kPairMinBlocks) step_kernel_pair(
     }
 }
 
+// ---- narrow batches ----------------------------------------------------------------------------------
+// A batch of at most 16 V columns (128 float16 or 64 float32 positions: one partly used tile) needs only
+// the first G x 16 bytes of each gathered 512-byte row line, G = the smallest power of two with G V >= batch.
+// The register kernel would still move whole lines; here the warp splits into S = 32 / G groups of G lanes
+// and each group gathers its own synapse, so one warp load brings S synapses (at B = 1, 32 synapses x 16
+// bytes).  A row's group sums are joined with log2 S shuffle steps and group 0 runs the row's epilogue for
+// its G V columns; columns past them are neither read nor written.  Inference only (the training backward
+// reads whole tiles of the saved state).  The sums are the same as the register kernel's up to their order.
+template <typename T, typename TV, int G>
+__global__ void __launch_bounds__(kWarps * 32, kMinBlocks) step_kernel_narrow(const StepArgs a) {
+    using Gt = Gather<T>;
+    constexpr int V = Gt::V;
+    constexpr int BT = 32 * V;
+    constexpr int S = 32 / G;                 // synapses per warp load
+    __shared__ float s_first[kWarps][G * V], s_last[kWarps][G * V];
+    __shared__ int s_bi[kWarps + 1], s_bj[kWarps + 1];
+    __shared__ LeanWarp s_w[kWarps];
+    __shared__ int s_r0, s_e0, s_nrows;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    {
+        const int item = __ldg(a.item_order + blockIdx.x);
+        if (tid <= kWarps) {
+            const int2 bd = __ldg(a.bounds + item * (kWarps + 1) + tid);
+            s_bi[tid] = bd.x;
+            s_bj[tid] = bd.y;
+        }
+        if (tid == 0) {
+            const int r0 = __ldg(a.item_rows + item);
+            s_r0 = r0;
+            s_e0 = __ldg(a.crow + r0);
+            s_nrows = __ldg(a.item_rows + item + 1) - r0;
+        }
+    }
+    __syncthreads();
+    auto cut = [&](int b) -> bool { return b >= 1 && b < kWarps && s_bj[b] > __ldg(a.crow + s_r0 + s_bi[b]) - s_e0; };
+    if (lane == 0) {
+        LeanWarp w;
+        w.is = s_bi[warp];
+        w.ie = s_bi[warp + 1];
+        w.js = s_bj[warp];
+        w.je = s_bj[warp + 1];
+        w.ilast = w.ie < s_nrows - 1 ? w.ie : s_nrows - 1;
+        w.flags = (cut(warp) ? 1 : 0) | (cut(warp + 1) ? 2 : 0);
+        s_w[warp] = w;
+    }
+    __syncwarp();
+
+    const char *x_base = static_cast<const char *>(a.x_in);            // the one tile
+    const int grp = lane / G;
+    const uint32_t lane_b = (uint32_t)(lane % G) * 16u;
+    const LeanWarp &me = s_w[warp];
+    for (int i = vld(me.is); i <= vld(me.ilast); ++i) {
+        int eb, ee;
+        {
+            const int r0 = vld(s_r0), e0 = vld(s_e0);
+            const int rs = __ldg(a.crow + r0 + i) - e0, re = __ldg(a.crow + r0 + i + 1) - e0;
+            const int js = vld(me.js), je = vld(me.je);
+            eb = rs > js ? rs : js;
+            ee = re < je ? re : je;
+        }
+        if (i == vld(me.ie) && ee <= eb) break;
+        float acc[V];
+#pragma unroll
+        for (int q = 0; q < V; ++q) acc[q] = 0.f;
+        for (int base = eb; base < ee; base += 32) {
+            const int n = ee - base < 32 ? ee - base : 32;
+            const int eoff = vld(s_e0) + base + lane;
+            int my_col = 0;
+            uint32_t my_val = 0u;
+            if (lane < n) {
+                my_col = __ldg(a.col + eoff);
+                my_val = Gt::bits_plain(static_cast<const TV *>(a.val) + eoff);
+            }
+            // uniform trip count: group g takes synapses k + u S + g of the window
+            for (int k = 0; k < n; k += S * kChunkR) {
+                uint4 x[kChunkR];
+#pragma unroll
+                for (int u = 0; u < kChunkR; ++u) {
+                    const int e = k + u * S + grp;
+                    const uint32_t c = (uint32_t)__shfl_sync(kFull, my_col, e & 31);
+                    x[u] = e < n ? __ldg(reinterpret_cast<const uint4 *>(x_base + (c * (uint32_t)(BT * sizeof(T)) + lane_b)))
+                                 : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int u = 0; u < kChunkR; ++u) Gt::fma(acc, __shfl_sync(kFull, my_val, (k + u * S + grp) & 31), x[u]);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o >= G; o >>= 1)
+#pragma unroll
+            for (int q = 0; q < V; ++q) acc[q] += __shfl_xor_sync(kFull, acc[q], o);
+        if (lane < G) {
+            const int flags = vld(me.flags);
+            const bool span_lo = (i == vld(me.is)) && (flags & 1), span_hi = (i == vld(me.ie)) && (flags & 2);
+            if (span_lo || span_hi) {
+                float *slot = span_lo ? s_first[warp] : s_last[warp];
+#pragma unroll
+                for (int q = 0; q < V; ++q) slot[lane * V + q] = acc[q];
+            } else if (i < vld(me.ie)) {
+                finish_row<T, BT>(a, vld(s_r0) + i, 0, lane * V, acc);
+            }
+        }
+    }
+    __syncthreads();
+    const int b = warp + 1;
+    if (lane < G && b < kWarps && cut(b)) {
+        int fb = b;
+        while (fb > 1 && s_bi[fb - 1] == s_bi[fb] && cut(fb - 1)) --fb;
+        if (fb == b) {
+            const int row = s_bi[b], off = lane * V;
+            float sum[V];
+#pragma unroll
+            for (int q = 0; q < V; ++q) sum[q] = s_last[b - 1][off + q];
+            for (int w = b;; ++w) {
+#pragma unroll
+                for (int q = 0; q < V; ++q) sum[q] += s_first[w][off + q];
+                if (!(w + 1 < kWarps && s_bi[w + 1] == row && cut(w + 1))) break;
+            }
+            finish_row<T, BT>(a, s_r0 + row, 0, off, sum);
+        }
+    }
+}
+
 // ---- a step without synapses ---------------------------------------------------------------------
 // R_{t-1} is empty (the first step): every row is the epilogue alone, y = k (+ drive).  One warp per
 // (row, tile), rows fastest, so consecutive warps write consecutive 512-byte lines of the tile.
@@ -527,13 +651,25 @@ void launch(const StepArgs &args, cudaStream_t s) {
     const int64_t blocks = tiles * a.n_items;
     AFB_CHECK(blocks < (1LL << 31), "grid too large: reduce the batch");
     // Short rows (configuration 3's step 2: 7.3 synapses per row) take the two-tile kernel; a step without
-    // synapses the epilogue alone.  All three give bitwise the same results.
+    // synapses the epilogue alone (all three give bitwise the same results); a narrow inference batch the
+    // narrow kernel (the same sums in another order).
     if (a.nnz == 0) {
         step_kernel_nosyn<T><<<grid_for((int64_t)a.n_rows * tiles * 32, 256, 148 * 64), 256, 0, s>>>(a, tiles);
     } else {
         // the gathers address a tile's slab with 32-bit byte offsets
         AFB_CHECK(a.ts_in * (int64_t)sizeof(T) <= (int64_t)UINT32_MAX, "a step's state tile exceeds 4 GB");
-        if (a.nnz < kShortRowDegree * (int64_t)a.n_rows) {
+        constexpr int V = Lane<T>::V;
+        if (!a.y_out && a.batch <= 16 * V) {          // a narrow inference batch: G lanes per synapse
+            const int g = a.batch <= V ? 1 : a.batch <= 2 * V ? 2 : a.batch <= 4 * V ? 4 : a.batch <= 8 * V ? 8 : 16;
+            const unsigned grid = (unsigned)a.n_items;
+            switch (g) {
+                case 1: step_kernel_narrow<T, TV, 1><<<grid, kWarps * 32, 0, s>>>(a); break;
+                case 2: step_kernel_narrow<T, TV, 2><<<grid, kWarps * 32, 0, s>>>(a); break;
+                case 4: step_kernel_narrow<T, TV, 4><<<grid, kWarps * 32, 0, s>>>(a); break;
+                case 8: step_kernel_narrow<T, TV, 8><<<grid, kWarps * 32, 0, s>>>(a); break;
+                default: step_kernel_narrow<T, TV, 16><<<grid, kWarps * 32, 0, s>>>(a); break;
+            }
+        } else if (a.nnz < kShortRowDegree * (int64_t)a.n_rows) {
             const int64_t pairs = (tiles + 1) / 2;
             step_kernel_pair<T, TV><<<(unsigned)(pairs * a.n_items), kWarps * 32, 0, s>>>(a);
         } else {

@@ -215,6 +215,24 @@ def test_ragged_batches_match_the_oracle(small, batch):
     assert orc.rel_l2(out16.cpu().numpy(), ref) < F16_GATE
 
 
+@pytest.mark.parametrize("batch", [1, 8, 9, 16, 17, 33, 64, 65, 100, 128, 129])
+def test_narrow_batches_equal_a_wide_run(small, batch):
+    """Batches of at most 128 float16 / 64 float32 positions take the narrow kernel (G lanes per synapse,
+    G = 1 .. 16); the same columns inside a 400-wide batch take the register kernel.  Columns are
+    independent, so the two agree up to the order of the float32 sums (float32 path) and one float16
+    rounding of the state (float16 path)."""
+    inst, rnn = small
+    u = torch.from_numpy(synth.drive(inst, 400, seed=batch + 3)).to(DEV)
+    in_idx, out_idx = inst.in_idx.to(DEV), inst.out_idx.to(DEV)
+    with torch.no_grad():
+        for dtype, tol in ((torch.float32, 1e-5), (torch.float16, 2e-3)):
+            wide = rnn.forward_io(u.to(dtype), in_idx, out_idx, 6)[:, :batch]
+            narrow = rnn.forward_io(u[:, :batch].contiguous().to(dtype), in_idx, out_idx, 6)
+            assert narrow.shape == (len(inst.out_idx), batch)
+            assert orc.rel_l2(narrow.double().cpu().numpy(), wide.double().cpu().numpy()) < tol, dtype
+    assert rnn.device_status() == 0
+
+
 @pytest.fixture(scope="module")
 def sparse():
     """Mean in-degree ~5: every light-cone step has short rows, so every step runs on the ring kernel."""
