@@ -71,3 +71,35 @@ def test_input_map_argument_errors_without_a_gpu():
         _lib.check(lib.afb_input_map_f16(10, 64, 838, p, 840, p, 840, p, 5.0, p, 32, None, None))
     with pytest.raises(_lib.AfbError, match="16-byte aligned"):
         _lib.check(lib.afb_input_map_f16(10, 64, 838, ctypes.c_void_p(258), 840, p, 840, p, 5.0, p, 64, None, None))
+
+
+def prototypes():
+    """{name: number of parameters} of every AFB_API declaration in include/afb.h."""
+    text = open(os.path.join(ROOT, "include", "afb.h")).read()
+    out = {}
+    for m in re.finditer(r"AFB_API\s+[\w\s\*]*?\b(afb_\w+)\s*\(([^)]*)\)", text):
+        params = " ".join(m.group(2).split())
+        out[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_bindings_take_as_many_arguments_as_the_header_declares():
+    from alphafly_b200 import _lib
+    protos = prototypes()
+    assert len(protos) == len(declared())
+    for name, n in protos.items():
+        assert len(_lib.SIGNATURES[name][1]) == n, name
+
+
+def test_gemm_argument_errors_are_reported_without_a_gpu():
+    from alphafly_b200 import _lib
+    lib = _lib.load()
+    args = [1.0, None, 1, 0, None, 1, 0, None, 0, 1.0, None, 1, None, 0, None, None]
+    with pytest.raises(_lib.AfbError, match="negative size"):
+        _lib.check(lib.afb_gemm_f32(-1, 1, 1, *args))
+    bad_bias = list(args)
+    bad_bias[8] = 3
+    with pytest.raises(_lib.AfbError, match="bias_dim"):
+        _lib.check(lib.afb_gemm_f32(1, 1, 1, *bad_bias))
+    assert lib.afb_gemm_f32(0, 5, 7, *args) == 0                      # an empty product is a no-op
+    assert lib.afb_gemm_workspace(0, 4, 4) == 0 and lib.afb_gemm_workspace(4, 4, 4) > 0
