@@ -198,8 +198,9 @@ class LightCone:
         return out
 
     def status(self, reset: bool = True) -> int:
-        """Device status word of this cone's step kernels: 0 = ok, 1 = a bounded wait gave up (some
-        forward since the last reset produced invalid output).  Synchronises the current stream."""
+        """Device status word of this cone's step kernels (``afb_cone_status``): 0 = ok; non-zero would
+        mean that a forward since the last reset produced invalid output.  Synchronises the current
+        stream."""
         st = ctypes.c_int(0)
         with torch.cuda.device(self.device):
             _lib.check(self._lib.afb_cone_status(self._h, ctypes.byref(st), int(reset), _stream(self.device)))

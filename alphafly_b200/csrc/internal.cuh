@@ -95,7 +95,7 @@ struct StepArgs {
     void *x_out;                   // state of R_t, tile-major
     int64_t ts_out;
     int64_t batch;
-    int *err;                      // device status word: set non-zero when a bounded wait gives up
+    int *err;                      // device status word (afb_cone_status); no current step kernel waits, so none sets it
     float *y_out;                  // training forward: pre-clamp drive of R_t, tile-major (float32 state only)
 };
 

@@ -140,9 +140,10 @@ AFB_API int afb_cone_forward_timed(const afb_cone *cone, int mode, const void *u
 AFB_API int afb_cone_forward_noalloc(const afb_cone *cone, int mode, const void *u_in, int64_t ld_u, int64_t batch,
                                      float *out, int64_t ld_out, void *stream);
 
-/* Device status of the handle's kernels, copied to *status (HOST): 0 = ok, 1 = a bounded wait of a
- * step kernel gave up (a gather never completed; that forward's output is not valid).  With reset != 0
- * the word is cleared.  Synchronous on `stream`. */
+/* Device status word of the handle's step kernels, copied to *status (HOST): 0 = ok; a non-zero value
+ * would mean that a step kernel's bounded wait gave up and that forward's output is not valid.  The
+ * current step kernels load their rows straight into registers and have no such waits, so the word stays
+ * 0; it is kept as part of the interface.  With reset != 0 the word is cleared.  Synchronous on `stream`. */
 AFB_API int afb_cone_status(const afb_cone *cone, int *status, int reset, void *stream);
 
 /* ---- training: forward with saved state, and backward -----------------------------------------
