@@ -26,6 +26,12 @@ def _device_status(dev: torch.device) -> torch.Tensor:
     return st
 
 
+def status_word(dev: torch.device) -> torch.Tensor | None:
+    """The device status word ``gemm`` passes to the library on ``dev`` (0 = ok; non-zero when a bounded
+    wait of the kernel gave up), or None before the first product on that device."""
+    return _status.get(dev)
+
+
 def _operand(t: torch.Tensor) -> tuple[torch.Tensor, int, int]:
     """(tensor, leading dimension, transposed) of a logical (rows, k) float32 matrix as the library reads it."""
     if t.stride(1) == 1 and t.stride(0) >= max(t.shape[1], 1):

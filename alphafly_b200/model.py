@@ -27,7 +27,7 @@ from . import _lib
 from .brain import ConnectomeRNN
 from .connectome import Connectome
 from .encoding import N_BASE, N_FEATURES, N_MOVES, move_squares
-from .gemm import affine
+from .gemm import affine, status_word
 
 READOUT_SUPERCLASSES = ("descending_neuron",)   # plus every efferent neuron (chessfly/model.py:23)
 
@@ -145,6 +145,22 @@ class FlyChessNet(nn.Module):
         st = getattr(self, "_status", None)
         if st is None or st.device != device:
             st = self._status = torch.zeros(1, dtype=torch.int32, device=device)
+        return st
+
+    def device_status(self, reset: bool = True) -> int:
+        """0 if every library kernel this network ran on its device since the last reset completed
+        normally: the light-cone step kernels (``brain.device_status``), the input map and the readout, and
+        the training products (``gemm.affine``).  Otherwise the first non-zero code: a bounded wait in a
+        kernel gave up and that call's output is not valid.  Reads device words, so it synchronises the
+        device's current stream; ``reset`` clears them."""
+        st = self.brain.device_status(reset)
+        dev = self.brain.pre.device
+        for word in (getattr(self, "_status", None), status_word(dev)):
+            if word is not None and word.device == dev:
+                v = int(word.item())
+                if reset and v:
+                    word.zero_()
+                st = st or v
         return st
 
     def brain_output(self, x: torch.Tensor) -> torch.Tensor:

@@ -339,6 +339,29 @@ def _tiny_net(**cfg):
     return FlyChessNet(synth.tiny(60, 600), ModelConfig(steps=3, **cfg)).to(DEV)
 
 
+def test_device_status_is_clear_after_inference_and_training():
+    """FlyChessNet.device_status gathers the status words of every library kernel the network ran (step
+    kernels, input map, readout, training products): 0 after a float16 inference forward through the
+    tensor-core readout and a training step, and a planted code (written on the host into the word) is
+    reported once, then cleared."""
+    from alphafly_b200.encoding import N_FEATURES
+    from alphafly_b200.train import Batch
+    net = _tiny_net()
+    g = torch.Generator().manual_seed(4)
+    x = (torch.rand(40, N_FEATURES, generator=g) < 0.05).float().to(DEV)
+    net.train()
+    batch = Batch(x, torch.randint(0, 4168, (40, 5), generator=g).to(DEV), torch.full((40, 5), 0.2).to(DEV),
+                  torch.ones(40, 5, dtype=torch.bool).to(DEV), torch.randint(0, 3, (40,), generator=g).to(DEV),
+                  torch.zeros(40).to(DEV))
+    train_step(net, make_optimizer(net, TrainConfig()), batch, DEV)
+    net.eval()
+    with torch.no_grad():
+        net(x)
+    assert net.device_status() == 0
+    net._map_status(DEV).fill_(4)
+    assert net.device_status() == 4 and net.device_status() == 0
+
+
 def test_factorised_policy_head_is_a_no_op_until_trained():
     """tests/test_core.py:394-416: with the zero-initialised from/to terms the network is its dense policy
     head on the normalised readout; an old checkpoint without those terms loads."""
